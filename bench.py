@@ -1,0 +1,384 @@
+#!/usr/bin/env python3
+"""Throughput of the Swin2SR forward pass: output megapixels per second.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload classical-x4]
+    python bench.py --impl reference ...        # the reference CPU path, host cores
+
+A step is one whole-image forward of the workload (default classical-x4: one
+240x320 image -> 960x1280, seeded weights and input, see workloads.py). Multi-GPU
+(torchrun, one process per GPU): every rank runs its own copy of the workload
+with no communication (replicas, weak scaling); the time is the max over ranks.
+
+Printed (rank 0, one JSON line): device-resident throughput (`value`, CUDA events
+on the launch stream, L2 flushed between steps outside the timed events), the
+end-to-end throughput through the public host API with host buffers (`e2e`),
+the dominant kernel's roofline, a bounded CPU-oracle baseline, and the SM clocks
+sampled during the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "output Mpix/s, classical-x4 whole image, 1/2/4/8 B200; % tensor/HBM peak"
+
+
+def _pkg():
+    if "swin2sr_b200" in sys.modules:
+        return sys.modules["swin2sr_b200"]
+    spec = importlib.util.spec_from_file_location(
+        "swin2sr_b200", ROOT / "swin2sr-rs_b200" / "__init__.py",
+        submodule_search_locations=[str(ROOT / "swin2sr-rs_b200")])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["swin2sr_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _oracle():
+    if str(ROOT) not in sys.path:
+        sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    if not O.LIB.exists():
+        O.build()
+    return O
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["bf16_tflops"], d["bf16_tflops_sustained"], d["hbm_gbs"], "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def kernel_flops(wt, B, hp, wp):
+    """Algorithmic FLOPs (2*MAC, real channel counts) per launch of each kernel class."""
+    T = B * hp * wp
+    C, m, s, F = wt.embed, wt.mlp_ratio, wt.scale, wt.feat
+    f = {
+        "gemm_qkv": 2 * T * C * 3 * C,
+        "window_attention": 2 * T * 2 * wt.window ** 2 * C,
+        "gemm_proj": 2 * T * C * C,
+        "gemm_fc1": 2 * T * C * m * C,
+        "gemm_fc2": 2 * T * m * C * C,
+        "conv_stage": 2 * T * 9 * C * C,
+        "gemm_stage_pe": 2 * T * C * C,
+        "gemm_stage_pe_norm": 2 * T * C * C,
+        "gemm_patch_embed": 2 * T * C * C,
+        "conv_after_body": 2 * T * 9 * C * C,
+        "conv_first": 2 * T * 27 * C,
+        "conv_before_upsample": 2 * T * 9 * C * F,
+        "conv_upsample0": 2 * T * 9 * F * 4 * F,
+        "conv_upsample1": 2 * 4 * T * 9 * F * 4 * F,
+        "conv_last": 2 * s * s * T * 9 * F * 3,
+    }
+    return f
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device, self.proc = device, None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            p = [v.strip() for v in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax.append(float(p[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def crop_for_budget(O, P, wt, x, seconds):
+    """Largest 3:4 crop of the workload image whose oracle forward fits `seconds`."""
+    _, _, H, W = x.shape
+    probe_h, probe_w = 32, 40
+    a = x[0, :, :probe_h, :probe_w]
+    O.forward(wt, probe_h, probe_w, a)
+    t = time.perf_counter()
+    O.forward(wt, probe_h, probe_w, a)
+    per_px = (time.perf_counter() - t) / ((probe_h // 8 + 1) * 8 * (probe_w // 8 + 1) * 8)
+    best = (probe_h, probe_w)
+    for k in range(1, 100):
+        hh, ww = 24 * k, 32 * k
+        if hh > H or ww > W:
+            break
+        if ((hh // 8 + 1) * 8) * ((ww // 8 + 1) * 8) * per_px <= seconds:
+            best = (hh, ww)
+    return best
+
+
+def run_reference(args):
+    """The reference's CPU path for this workload, on the host cores (the oracle port:
+    the Rust reference does not build here - no cargo, lightgpu not vendored)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    P = _pkg()
+    wl = importlib.import_module("swin2sr_b200.workloads")
+    O = _oracle()
+    cores = os.cpu_count() or 1
+    O.set_threads(cores)
+    spec = wl.WORKLOADS[args.workload]
+    wt = P.weights.Weights.seeded(spec["task"], 0)
+    x = wl.adjust(wl.make_input(args.workload, 1), wt)
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    hh, ww = crop_for_budget(O, P, wt, x, budget)
+    a = np.ascontiguousarray(x[0, :, :hh, :ww])
+    for _ in range(args.warmup):
+        O.forward(wt, hh, ww, a)
+    ts = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        O.forward(wt, hh, ww, a)
+        ts.append(time.perf_counter() - t)
+    mp = hh * wt.scale * ww * wt.scale / 1e6
+    value = mp / statistics.mean(ts)
+    sample = (f"{hh}x{ww} crop of the {args.workload} input per step (one forward, "
+              f"{hh * wt.scale}x{ww * wt.scale} output); seed-0 weights")
+    line = {
+        "metric": METRIC, "value": round(value, 5), "unit": "Mpix/s", "impl": "reference",
+        "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * statistics.mean(ts), 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "sample": sample,
+                   "implementation": "C++ restatement of swin2sr-rs src/cpu.rs (oracle/)"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "Mpix/s", "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": "Mpix/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="classical-x4")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    P = _pkg()
+    capi = importlib.import_module("swin2sr_b200.capi")
+    wl = importlib.import_module("swin2sr_b200.workloads")
+    spec = wl.WORKLOADS[args.workload]
+    wt = P.weights.Weights.seeded(spec["task"], 0)
+    B, h, w, s = spec["batch"], spec["h"], spec["w"], wt.scale
+    win = wt.window
+    hp, wp = (h // win + 1) * win, (w // win + 1) * win
+    x = wl.make_input(args.workload)
+    xa = wl.adjust(x, wt)
+    handle = capi.Handle(wt, device=local)
+
+    dev = torch.device("cuda", local)
+    d_in = torch.from_numpy(xa).to(dev)
+    d_out = torch.empty((B, 3, h * s, w * s), dtype=torch.float32, device=dev)
+    d_aux = torch.empty((B, 3, hp, wp), dtype=torch.float32, device=dev) \
+        if wt.upsampler == "pixelshuffle_aux" else None
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def step():
+        handle.forward_device(B, h, w, d_in.data_ptr(), d_out.data_ptr(),
+                              d_aux.data_ptr() if d_aux is not None else 0, sp)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    # One profiled, untimed step: per-kernel-class event times, to pick the dominant one.
+    handle.profile(True)
+    step()
+    torch.cuda.synchronize(dev)
+    prof = handle.profile_report(reset=True)
+    handle.profile(False)
+    dominant = max(prof, key=lambda k: prof[k][1])
+
+    # ---------------------------------------------------------------- timed region
+    handle.profile(True, only=dominant)
+    clocks = ClockSampler(local)
+    launches0 = handle.launch_count()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(args.steps):
+        flush.zero_()                      # L2 flush between steps, outside the events
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    launches = handle.launch_count() - launches0
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    dom = handle.profile_report(reset=True).get(dominant, (0, 0.0))
+    handle.profile(False)
+    total_ms = float(sum(step_ms))
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    out_mpix = B * h * s * w * s / 1e6
+    value = world * out_mpix / (ms_per_step / 1e3)
+
+    # ---------------------------------------------------------------- end to end
+    pin_in = torch.empty((B, 3, h, w), dtype=torch.float32).pin_memory().numpy()
+    pin_out = torch.empty((B, 3, h * s, w * s), dtype=torch.float32).pin_memory().numpy()
+    mean = np.asarray(wt.mean, np.float32)[None, :, None, None]
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        np.subtract(x, mean, out=pin_in)          # Pre::adjust on the host
+        pin_in *= np.float32(wt.img_range)
+        handle._check(handle.L.s2s_forward_batch(handle.h, B, h, w, capi._fp(pin_in),
+                                                 capi._fp(pin_out), None))
+
+    e2e_step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * out_mpix / e2e_s
+
+    # ---------------------------------------------------------------- roofline
+    pk_burst, pk_sus, hbm, pk_kind = peaks()
+    flops = kernel_flops(wt, B, hp, wp).get(dominant)
+    roofline = None
+    if flops and dom[0] > 0:
+        per_launch_s = dom[1] / dom[0] / 1e3
+        achieved = flops / per_launch_s / 1e12
+        traffic = None
+        tf = ROOT / "profiles" / "traffic.json"
+        if tf.exists():
+            try:
+                traffic = json.loads(tf.read_text()).get(args.workload, {}).get(dominant)
+            except (ValueError, AttributeError):
+                traffic = None
+        roofline = {"kernel": dominant, "bound": "tensor", "achieved": round(achieved, 2),
+                    "peak": pk_burst, "unit": "TFLOP/s", "frac": round(achieved / pk_burst, 4),
+                    "peak_kind": f"bf16 dense burst ({pk_kind})", "traffic": traffic,
+                    "flops_per_launch": flops, "launches": dom[0],
+                    "avg_launch_ms": round(dom[1] / dom[0], 4)}
+    whole_flops = wt.flops_forward(hp, wp, B)
+    whole = {"tflops": round(whole_flops / (ms_per_step / 1e3) / 1e12, 2),
+             "frac_of_bf16_peak": round(whole_flops / (ms_per_step / 1e3) / 1e12 / pk_burst, 4)}
+
+    # ---------------------------------------------------------------- CPU baseline
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        O = _oracle()
+        cores = os.cpu_count() or 1
+        O.set_threads(cores)
+        hh, ww = crop_for_budget(O, P, wt, xa, 12.0)
+        a = np.ascontiguousarray(xa[0, :, :hh, :ww])
+        t = time.perf_counter()
+        O.forward(wt, hh, ww, a)
+        dt = time.perf_counter() - t
+        cpu = {"value": round(hh * s * ww * s / 1e6 / dt, 5), "unit": "Mpix/s", "cores": cores,
+               "kind": "port",
+               "sample": f"one forward of a {hh}x{ww} crop of the {args.workload} input "
+                         f"({dt:.1f} s), C++ restatement of src/cpu.rs, {cores} threads"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "Mpix/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {"workload": args.workload, "batch_per_gpu": B, "input": f"{h}x{w}",
+                       "output": f"{h * s}x{w * s}", "padded_plane": f"{hp}x{wp}",
+                       "weights": "seeded random init (seed 0)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": "flushed between steps (256 MB write, outside the events)",
+                       "precision": "fp16 operands, fp32 accumulate/residual/norms"},
+            "e2e": {"value": round(e2e_value, 3), "unit": "Mpix/s",
+                    "h2d_bytes_per_step": int(B * 3 * h * w * 4),
+                    "d2h_bytes_per_step": int(B * 3 * h * s * w * s * 4)},
+            "roofline": roofline, "whole_forward": whole, "cpu_baseline": cpu,
+            "gpu_launches": int(launches), "clocks": clk,
+            "kernel_ms_per_step": {k: round(v[1], 4) for k, v in sorted(
+                prof.items(), key=lambda kv: -kv[1][1])},
+        }
+        print(json.dumps(line), flush=True)
+    handle.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

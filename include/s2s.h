@@ -1,0 +1,149 @@
+/* s2s.h - C ABI of the B200-native Swin2SR forward pass.
+ *
+ * This is the boundary the reference's GPU backend plugs into: swin2sr-rs
+ * src/gpu.rs implements `Backend` (src/backend.rs:29-49) for `Gpu`; a drop-in
+ * `Gpu` keeps that trait impl and forwards to these entry points (the binding a
+ * maintainer adds is in INTEGRATION.md). Plain C types only; every pointer is
+ * caller-owned unless stated.
+ *
+ * Threading: a handle is not thread-safe (the reference's `forward` takes
+ * `&mut self`); one CUDA stream per handle; the host-buffer calls return when the
+ * result is on the host.
+ */
+#ifndef S2S_H
+#define S2S_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The reference reports errors as `Result<_, String>` and its CLI
+ * retries with a smaller tile only when the message contains "OUT_OF_MEMORY"
+ * (src/main.rs:660-662): S2S_ERR_OOM's message always contains
+ * "CUDA_ERROR_OUT_OF_MEMORY" so that retry keeps working. */
+enum {
+  S2S_OK = 0,
+  S2S_ERR_OOM = 1,         /* device allocation failed */
+  S2S_ERR_INVALID = 2,     /* bad argument, shape or missing tensor */
+  S2S_ERR_CUDA = 3,        /* any other CUDA error */
+  S2S_ERR_NCCL = 4,        /* collective failure (sharded modes) */
+  S2S_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up */
+  S2S_ERR_UNSUPPORTED = 6  /* architecture this build does not implement */
+};
+
+/* Reconstruction heads (src/weights.rs:18-29, Upsampler). */
+enum {
+  S2S_PIXELSHUFFLE = 0,
+  S2S_PIXELSHUFFLEDIRECT = 1,
+  S2S_NEARESTCONV = 2,
+  S2S_PIXELSHUFFLE_AUX = 3
+};
+
+/* The architecture, as the checkpoint's __metadata__ states it
+ * (src/weights.rs:94-137; tools/convert.py:224-236). */
+typedef struct s2s_config {
+  int upsampler;     /* S2S_PIXELSHUFFLE ... */
+  int scale;         /* 2 or 4 */
+  int window;        /* 8 */
+  int embed;         /* 60 or 180 */
+  int heads;         /* attention heads per block */
+  int mlp_ratio;     /* 2 */
+  int n_depths;      /* RSTB stages */
+  int depths[16];    /* blocks per stage */
+  float img_range;   /* 1.0 */
+  float mean[3];     /* RGB mean subtracted before the network */
+} s2s_config;
+
+/* One converted-checkpoint tensor, row-major fp32, borrowed for the call only
+ * (the reference hands out `&[f32]` views of its mmap, src/weights.rs:240-242).
+ * Names are tools/convert.py's: "layers.{s}.residual_group.blocks.{b}.attn.qkv.wq",
+ * ".attn.cpb_pre", "conv_first.weight", ... */
+typedef struct s2s_tensor {
+  const char* name;
+  const float* data;
+  int ndim;
+  int64_t shape[4];
+} s2s_tensor;
+
+typedef struct s2s_handle s2s_handle;
+
+/* Gpu::new (src/gpu.rs:101-125): validate, repack every needed tensor to the
+ * device layouts (fp16 K-major GEMM operands, fp32 biases / norms / bias table)
+ * and upload them once. `device` is the CUDA ordinal. On failure *out is NULL
+ * and the message is available from s2s_last_error(NULL). */
+int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, int device,
+               s2s_handle** out);
+
+/* Backend::forward (src/backend.rs:34; src/gpu.rs:741-754): `in_chw` is
+ * [3][h][w] fp32 ALREADY mean-adjusted by Pre::adjust (src/backend.rs:76-86) and
+ * unpadded; the library pads (src/plan.rs:116-139), runs the network and writes
+ * `out_chw` = [3][h*scale][w*scale], denormalised and cropped, not clamped
+ * (src/cpu.rs:1925-1941). `aux_chw` may be NULL; for the pixelshuffle_aux head it
+ * receives [3][hp][wp] (s2s_aux_dims), denormalised and NOT cropped
+ * (src/cpu.rs:1892-1903). Host buffers; synchronous. */
+int s2s_forward(s2s_handle* h, int height, int width, const float* in_chw, float* out_chw,
+                float* aux_chw);
+
+/* The same for `batch` independent images of one size, contiguous
+ * [batch][3][h][w] -> [batch][3][h*s][w*s] (+ [batch][3][hp][wp] aux). */
+int s2s_forward_batch(s2s_handle* h, int batch, int height, int width, const float* in,
+                      float* out, float* aux);
+
+/* Device-resident variant: pointers are device memory on the handle's device,
+ * work is enqueued on `stream` (a cudaStream_t; NULL = the handle's own stream)
+ * and the call returns without synchronising. */
+int s2s_forward_device(s2s_handle* h, int batch, int height, int width, const float* d_in,
+                       float* d_out, float* d_aux, void* stream);
+
+/* Backend::aux geometry: the padded plane of an h x w input (src/plan.rs:39-47).
+ * Returns S2S_ERR_INVALID for heads without an aux image. */
+int s2s_aux_dims(const s2s_handle* h, int height, int width, int* aux_h, int* aux_w);
+
+/* gpu::uploaded_bytes (src/gpu.rs:792-799): device bytes held by the weights. */
+int64_t s2s_uploaded_bytes(const s2s_handle* h);
+
+/* per_pixel_floats(gpu = true) (src/backend.rs:300-383), made exact: the
+ * activation bytes a forward of `batch` h x w images allocates. */
+int64_t s2s_workspace_bytes(const s2s_handle* h, int batch, int height, int width);
+
+/* The last error message of `h` (or of the last failed s2s_create when h is NULL). */
+const char* s2s_last_error(const s2s_handle* h);
+
+/* Per-launch CUDA-event timing, the SWIN2SR_PROFILE_GPU profiler
+ * (src/cuda.rs:109-140, 163-259). The environment variable turns it on at
+ * create time; this toggles it at run time. Events are recorded on the stream
+ * each kernel is launched on. `only` (may be NULL) restricts timing to kernel
+ * classes whose name starts with it, so a timed run pays for two events per
+ * launch of that class only. */
+int s2s_profile_enable(s2s_handle* h, int on, const char* only);
+
+/* Aggregated profile since the last reset, one line per kernel class:
+ * "name launches total_ms". Writes at most `cap` bytes (NUL-terminated) and
+ * returns the length needed. Resets the counters when `reset` is non-zero. */
+int s2s_profile_report(s2s_handle* h, char* buf, int cap, int reset);
+
+/* Kernel launches enqueued by this handle since creation. */
+int64_t s2s_launch_count(const s2s_handle* h);
+
+/* Diagnostics (the counterpart of the reference's `dump` hooks, src/cpu.rs:1405,
+ * 1453-1459, which name every activation for bisection against the torch
+ * network): stop the next forwards after `launches` kernel launches (-1 = run
+ * to the end), and read a named workspace buffer of the current plan back as
+ * fp32 ("P", "F0", "F0h", "X0", "X1", "X16_0", "X16_1", "S", "QKV", "AO", "H16",
+ * "HA", "HB0", "HB1", "HB2", "BIC", "BICF", "AUXRAW"). s2s_debug_read returns
+ * the element count, or -1 for an unknown name / no plan. */
+int s2s_debug_stop_after(s2s_handle* h, int64_t launches);
+int64_t s2s_debug_read(s2s_handle* h, const char* buffer, float* host, int64_t capacity);
+
+void s2s_destroy(s2s_handle* h);
+
+const char* s2s_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* S2S_H */

@@ -1,0 +1,210 @@
+"""ctypes binding of the C ABI in include/s2s.h (libs2s.so, built by build.py).
+
+This is the same binding a Rust maintainer writes with `extern "C"` blocks: plain
+structs, plain pointers. The library MUST be present: there is no CPU fallback,
+and loading fails loudly when libs2s.so has not been built.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libs2s.so"
+
+S2S_OK, S2S_ERR_OOM, S2S_ERR_INVALID, S2S_ERR_CUDA, S2S_ERR_NCCL, S2S_ERR_TIMEOUT, \
+    S2S_ERR_UNSUPPORTED = range(7)
+STATUS_NAMES = {0: "S2S_OK", 1: "S2S_ERR_OOM", 2: "S2S_ERR_INVALID", 3: "S2S_ERR_CUDA",
+                4: "S2S_ERR_NCCL", 5: "S2S_ERR_TIMEOUT", 6: "S2S_ERR_UNSUPPORTED"}
+UPSAMPLER_CODE = {"pixelshuffle": 0, "pixelshuffledirect": 1, "nearest+conv": 2,
+                  "pixelshuffle_aux": 3}
+
+# Every entry point include/s2s.h declares.
+EXPORTS = ("s2s_create", "s2s_forward", "s2s_forward_batch", "s2s_forward_device",
+           "s2s_aux_dims", "s2s_uploaded_bytes", "s2s_workspace_bytes", "s2s_last_error",
+           "s2s_profile_enable", "s2s_profile_report", "s2s_launch_count", "s2s_destroy",
+           "s2s_version", "s2s_debug_stop_after", "s2s_debug_read")
+
+
+class S2SConfig(ctypes.Structure):
+    _fields_ = [("upsampler", ctypes.c_int), ("scale", ctypes.c_int), ("window", ctypes.c_int),
+                ("embed", ctypes.c_int), ("heads", ctypes.c_int), ("mlp_ratio", ctypes.c_int),
+                ("n_depths", ctypes.c_int), ("depths", ctypes.c_int * 16),
+                ("img_range", ctypes.c_float), ("mean", ctypes.c_float * 3)]
+
+
+class S2STensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("data", ctypes.POINTER(ctypes.c_float)),
+                ("ndim", ctypes.c_int), ("shape", ctypes.c_int64 * 4)]
+
+
+class S2SError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load libs2s.so, declaring every prototype. Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise FileNotFoundError(
+            f"{LIB_PATH} is missing: build it with `python swin2sr-rs_b200/build.py` "
+            f"(there is no CPU fallback for the forward pass)")
+    L = ctypes.CDLL(str(LIB_PATH))
+    fp = ctypes.POINTER(ctypes.c_float)
+    vp = ctypes.c_void_p
+    L.s2s_create.argtypes = [ctypes.POINTER(S2SConfig), ctypes.POINTER(S2STensor), ctypes.c_int,
+                             ctypes.c_int, ctypes.POINTER(vp)]
+    L.s2s_create.restype = ctypes.c_int
+    L.s2s_forward.argtypes = [vp, ctypes.c_int, ctypes.c_int, fp, fp, fp]
+    L.s2s_forward.restype = ctypes.c_int
+    L.s2s_forward_batch.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, fp, fp, fp]
+    L.s2s_forward_batch.restype = ctypes.c_int
+    L.s2s_forward_device.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp]
+    L.s2s_forward_device.restype = ctypes.c_int
+    L.s2s_aux_dims.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                               ctypes.POINTER(ctypes.c_int)]
+    L.s2s_aux_dims.restype = ctypes.c_int
+    L.s2s_uploaded_bytes.argtypes = [vp]
+    L.s2s_uploaded_bytes.restype = ctypes.c_int64
+    L.s2s_workspace_bytes.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.s2s_workspace_bytes.restype = ctypes.c_int64
+    L.s2s_last_error.argtypes = [vp]
+    L.s2s_last_error.restype = ctypes.c_char_p
+    L.s2s_profile_enable.argtypes = [vp, ctypes.c_int, ctypes.c_char_p]
+    L.s2s_profile_enable.restype = ctypes.c_int
+    L.s2s_profile_report.argtypes = [vp, ctypes.c_char_p, ctypes.c_int, ctypes.c_int]
+    L.s2s_profile_report.restype = ctypes.c_int
+    L.s2s_launch_count.argtypes = [vp]
+    L.s2s_launch_count.restype = ctypes.c_int64
+    L.s2s_destroy.argtypes = [vp]
+    L.s2s_destroy.restype = None
+    L.s2s_debug_stop_after.argtypes = [vp, ctypes.c_int64]
+    L.s2s_debug_stop_after.restype = ctypes.c_int
+    L.s2s_debug_read.argtypes = [vp, ctypes.c_char_p, fp, ctypes.c_int64]
+    L.s2s_debug_read.restype = ctypes.c_int64
+    L.s2s_version.argtypes = []
+    L.s2s_version.restype = ctypes.c_char_p
+    _lib = L
+    return L
+
+
+def _fp(a):
+    return a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+def config_of(wt) -> S2SConfig:
+    cfg = S2SConfig()
+    cfg.upsampler = UPSAMPLER_CODE[wt.upsampler]
+    cfg.scale, cfg.window, cfg.embed = wt.scale, wt.window, wt.embed
+    cfg.heads, cfg.mlp_ratio, cfg.n_depths = wt.heads, wt.mlp_ratio, len(wt.depths)
+    for i, d in enumerate(wt.depths):
+        cfg.depths[i] = d
+    cfg.img_range = wt.img_range
+    for i in range(3):
+        cfg.mean[i] = wt.mean[i]
+    return cfg
+
+
+class Handle:
+    """One s2s_handle on one device."""
+
+    def __init__(self, wt, device: int = 0):
+        L = load()
+        self.L, self.wt, self.device = L, wt, device
+        names = wt.needed()
+        arr = (S2STensor * len(names))()
+        keep = []
+        for i, n in enumerate(names):
+            a = np.ascontiguousarray(wt.t(n), dtype=np.float32)
+            keep.append((n.encode(), a))
+            arr[i].name = keep[-1][0]
+            arr[i].data = _fp(a)
+            arr[i].ndim = a.ndim
+            for d in range(min(a.ndim, 4)):
+                arr[i].shape[d] = a.shape[d]
+        h = ctypes.c_void_p()
+        rc = L.s2s_create(ctypes.byref(config_of(wt)), arr, len(names), device, ctypes.byref(h))
+        if rc != S2S_OK:
+            raise S2SError(rc, L.s2s_last_error(None).decode())
+        self.h = h
+
+    def _check(self, rc):
+        if rc != S2S_OK:
+            raise S2SError(rc, self.L.s2s_last_error(self.h).decode())
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.s2s_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def aux_dims(self, h: int, w: int):
+        ah, aw = ctypes.c_int(), ctypes.c_int()
+        self._check(self.L.s2s_aux_dims(self.h, h, w, ctypes.byref(ah), ctypes.byref(aw)))
+        return ah.value, aw.value
+
+    def forward_batch(self, x: np.ndarray):
+        """[B][3][h][w] mean-adjusted -> ([B][3][h*s][w*s], aux [B][3][hp][wp] or None)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        B, _, h, w = x.shape
+        s, win = self.wt.scale, self.wt.window
+        out = np.empty((B, 3, h * s, w * s), np.float32)
+        aux = None
+        if self.wt.upsampler == "pixelshuffle_aux":
+            aux = np.empty((B, 3, (h // win + 1) * win, (w // win + 1) * win), np.float32)
+        self._check(self.L.s2s_forward_batch(self.h, B, h, w, _fp(x), _fp(out),
+                                             _fp(aux) if aux is not None else None))
+        return out, aux
+
+    def forward_device(self, B, h, w, d_in: int, d_out: int, d_aux: int = 0, stream: int = 0):
+        self._check(self.L.s2s_forward_device(self.h, B, h, w, ctypes.c_void_p(d_in),
+                                              ctypes.c_void_p(d_out), ctypes.c_void_p(d_aux or None),
+                                              ctypes.c_void_p(stream or None)))
+
+    def uploaded_bytes(self) -> int:
+        return int(self.L.s2s_uploaded_bytes(self.h))
+
+    def workspace_bytes(self, B, h, w) -> int:
+        return int(self.L.s2s_workspace_bytes(self.h, B, h, w))
+
+    def profile(self, on: bool = True, only: str | None = None):
+        self._check(self.L.s2s_profile_enable(self.h, 1 if on else 0,
+                                              only.encode() if only else None))
+
+    def profile_report(self, reset: bool = True) -> dict:
+        n = self.L.s2s_profile_report(self.h, None, 0, 0)
+        buf = ctypes.create_string_buffer(max(n, 1))
+        self.L.s2s_profile_report(self.h, buf, n, 1 if reset else 0)
+        out = {}
+        for line in buf.value.decode().splitlines():
+            name, cnt, ms = line.split()
+            out[name] = (int(cnt), float(ms))
+        return out
+
+    def debug_stop_after(self, launches: int):
+        self._check(self.L.s2s_debug_stop_after(self.h, int(launches)))
+
+    def debug_read(self, name: str) -> np.ndarray:
+        n = self.L.s2s_debug_read(self.h, name.encode(), None, 0)
+        if n < 0:
+            raise KeyError(name)
+        out = np.empty(n, np.float32)
+        self.L.s2s_debug_read(self.h, name.encode(), _fp(out), n)
+        return out
+
+    def launch_count(self) -> int:
+        return int(self.L.s2s_launch_count(self.h))

@@ -1,0 +1,83 @@
+// Host/device interface of the tcgen05 GEMM / implicit-GEMM 3x3 convolution.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace s2s {
+
+enum Act : int { ACT_NONE = 0, ACT_GELU = 1, ACT_LRELU = 2 };
+
+// Where the epilogue writes.
+enum Store : int {
+  STORE_ROWS = 0,      // row-major rows (optionally through a row map), fp32 and/or fp16
+  STORE_SHUFFLE2 = 1,  // conv output pixel-shuffled by 2 into an NHWC fp16 plane (columns
+                       // ordered (dy, dx, f)), optional fp32 residual at the destination
+  STORE_PLANES = 2,    // first 3 columns -> NCHW fp32 planes: denormalised+cropped and/or raw
+  STORE_DIRECT = 3,    // pixelshuffledirect: column ch*s*s + dy*s + dx -> denormalised NCHW
+};
+
+struct Epi {
+  const float* bias;  // padded to the full N, or null
+  int act;
+  float slope;
+  // fp32 residual added after the activation (before a LayerNorm), indexed by the
+  // tile's logical row and the global column; thread-per-row reads.
+  const float* res_pre;
+  int ld_res_pre;
+  // LayerNorm over the first ln_n columns (ln_n == 0: off). Requires one N tile.
+  const float* ln_g;
+  const float* ln_b;
+  int ln_n;
+  float ln_eps;
+  // fp32 residual added last (STORE_ROWS: at the logical row; STORE_SHUFFLE2: at
+  // the destination pixel).
+  const float* res_post;
+  int ld_res_post;
+  // Columns [n_valid, N) are written as zero.
+  int n_valid;
+  // Outputs (STORE_ROWS / STORE_SHUFFLE2).
+  float* o32;
+  int ld32;
+  const int* map32;
+  float* o32b;
+  int ld32b;
+  const int* map32b;
+  __half* o16;
+  int ld16;
+  const int* map16;
+  int store;
+  // STORE_PLANES / STORE_DIRECT
+  float* planes;      // denormalised, cropped to crop_h x crop_w (x scale for DIRECT)
+  float* planes_raw;  // raw, uncropped [B][3][H][W]
+  int crop_h, crop_w, scale;
+  float img_range;
+  float mean0, mean1, mean2;
+};
+
+struct GemmArgs {
+  int M, N, K;  // rows (GEMM mode), padded N, padded K (multiple of 64)
+  int conv;     // 0: A is [M][K]; 1: A is the NHWC plane of a 3x3 convolution
+  int H, W, B;  // conv plane (output geometry == input geometry)
+  int boxw, boxh, tiles_x, tiles_y;
+  int kc;  // conv: 64-channel chunks per tap
+  Epi epi;
+};
+
+// Launch D = A * B^T (+ epilogue). mapA / mapB are TMA descriptors built by
+// make_map_* below. BN is the N tile (<= 256, multiple of 32).
+cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& a,
+                        int BN, cudaStream_t st);
+
+// TMA descriptor helpers (driver entry point resolved at first use).
+bool make_map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols_padded,
+                   uint32_t box_rows);
+bool make_map_nhwc(CUtensorMap* m, const void* base, int B, int H, int W, int Cp, int boxw,
+                   int boxh);
+
+// The M tile of a convolution over a W-wide plane: box width = the largest power
+// of two <= 128 dividing W.
+void conv_box(int W, int* boxw, int* boxh);
+
+}  // namespace s2s

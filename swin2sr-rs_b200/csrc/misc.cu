@@ -1,0 +1,177 @@
+// The HBM-bound pieces around the tensor-core kernels: reflect padding of the
+// input plane, the 3-input-channel convolutions (conv_first, conv_after_aux,
+// conv_bicubic), the bicubic resample of the compressed head, and the nearest
+// x2 upsample of the real-world head.
+#include "common.cuh"
+
+namespace s2s {
+namespace {
+
+// src/plan.rs:116-139: [B][c][h][w] -> [B][c][hp][wp], whole-plane mirror.
+__global__ void k_pad_reflect(const float* __restrict__ x, float* __restrict__ y, int B, int c,
+                              int h, int w, int hp, int wp) {
+  const size_t n = (size_t)B * c * hp * wp;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int xx = (int)(i % wp);
+    const int yy = (int)((i / wp) % hp);
+    const size_t bc = i / ((size_t)wp * hp);
+    const int sy = yy < h ? yy : 2 * h - 1 - min(yy, 2 * h - 1);
+    const int sx = xx < w ? xx : 2 * w - 1 - min(xx, 2 * w - 1);
+    y[i] = x[(bc * h + sy) * w + sx];
+  }
+}
+
+// 3x3 s1 p1 conv with 3 input channels, NCHW fp32 input -> NHWC outputs.
+// Thread = (pixel, output channel), channel fastest, so stores are contiguous.
+// Taps in the oracle's order: bias first, then ky, kx, ci.
+__global__ void k_conv3_small(const float* __restrict__ in, const float* __restrict__ wgt,
+                              const float* __restrict__ bias, int B, int H, int W, int co_n,
+                              int act, float slope, float* __restrict__ o32, int ld32,
+                              __half* __restrict__ o16, int ld16) {
+  __shared__ float sw[256 * 27];
+  __shared__ float sb[256];
+  for (int i = threadIdx.x; i < co_n * 27; i += blockDim.x) sw[i] = wgt[i];
+  for (int i = threadIdx.x; i < co_n; i += blockDim.x) sb[i] = bias[i];
+  __syncthreads();
+  const size_t n = (size_t)B * H * W * co_n;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int co = (int)(i % co_n);
+    const size_t p = i / co_n;
+    const int x = (int)(p % W);
+    const int y = (int)((p / W) % H);
+    const int b = (int)(p / ((size_t)W * H));
+    float acc = sb[co];
+    const float* wc = sw + co * 27;
+#pragma unroll
+    for (int ky = 0; ky < 3; ky++) {
+      const int sy = y + ky - 1;
+      if (sy < 0 || sy >= H) continue;
+#pragma unroll
+      for (int kx = 0; kx < 3; kx++) {
+        const int sx = x + kx - 1;
+        if (sx < 0 || sx >= W) continue;
+#pragma unroll
+        for (int ci = 0; ci < 3; ci++)
+          acc += wc[ci * 9 + ky * 3 + kx] * in[(((size_t)b * 3 + ci) * H + sy) * W + sx];
+      }
+    }
+    if (act == 2 && acc < 0.0f) acc *= slope;
+    if (o32) o32[p * ld32 + co] = acc;
+    if (o16) o16[p * ld16 + co] = __float2half_rn(acc);
+  }
+}
+
+// Zero the pad channels [c0, ld) of NHWC rows (so padded K lanes are finite zeros).
+__global__ void k_zero_cols_f16(__half* __restrict__ x, size_t rows, int c0, int ld) {
+  const int w = ld - c0;
+  const size_t n = rows * w;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    x[(i / w) * ld + c0 + (i % w)] = __float2half_rn(0.0f);
+}
+
+// src/cpu.rs:877-935: torch bicubic, a = -0.75, align_corners = False, edge clamp.
+__device__ __forceinline__ float cubic_w(float t) {
+  const float A = -0.75f;
+  t = fabsf(t);
+  if (t <= 1.0f) return ((A + 2.0f) * t - (A + 3.0f)) * t * t + 1.0f;
+  if (t < 2.0f) return (((t - 5.0f) * t + 8.0f) * t - 4.0f) * A;
+  return 0.0f;
+}
+
+__global__ void k_bicubic(const float* __restrict__ in, float* __restrict__ out, int BC, int h,
+                          int w, int oh, int ow) {
+  const size_t n = (size_t)BC * oh * ow;
+  const float ry = (float)h / (float)oh, rx = (float)w / (float)ow;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int x = (int)(i % ow);
+    const int y = (int)((i / ow) % oh);
+    const size_t bc = i / ((size_t)ow * oh);
+    const float sy = ((float)y + 0.5f) * ry - 0.5f, sx = ((float)x + 0.5f) * rx - 0.5f;
+    const float by = floorf(sy), bx = floorf(sx);
+    int iy[4], ix[4];
+    float wy[4], wx[4];
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      iy[m] = min(max((int)by - 1 + m, 0), h - 1);
+      ix[m] = min(max((int)bx - 1 + m, 0), w - 1);
+      wy[m] = cubic_w(sy - (by + (float)m - 1.0f));
+      wx[m] = cubic_w(sx - (bx + (float)m - 1.0f));
+    }
+    const float* src = in + bc * h * w;
+    float acc = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+      const float* r = src + (size_t)iy[m] * w;
+      const float a0 = wx[0] * r[ix[0]], a1 = wx[1] * r[ix[1]];
+      const float a2 = wx[2] * r[ix[2]], a3 = wx[3] * r[ix[3]];
+      acc += wy[m] * ((a0 + a1) + (a2 + a3));
+    }
+    out[i] = acc;
+  }
+}
+
+// Nearest x2 upsample of an NHWC fp16 plane, 16 bytes per thread.
+__global__ void k_up2_nhwc(const __half* __restrict__ in, __half* __restrict__ out, int B, int H,
+                           int W, int C) {
+  const int cv = C / 8;
+  const size_t n = (size_t)B * 2 * H * 2 * W * cv;
+  const uint4* src = reinterpret_cast<const uint4*>(in);
+  uint4* dst = reinterpret_cast<uint4*>(out);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % cv);
+    const size_t p = i / cv;
+    const int x = (int)(p % (2 * W));
+    const int y = (int)((p / (2 * W)) % (2 * H));
+    const int b = (int)(p / ((size_t)4 * W * H));
+    dst[i] = src[(((size_t)b * H + (y >> 1)) * W + (x >> 1)) * cv + c];
+  }
+}
+
+inline unsigned grid_for(size_t n, int block) {
+  size_t g = (n + block - 1) / block;
+  if (g > 148 * 64) g = 148 * 64;
+  return (unsigned)(g == 0 ? 1 : g);
+}
+
+}  // namespace
+
+cudaError_t launch_pad_reflect(const float* x, float* y, int B, int c, int h, int w, int hp,
+                               int wp, cudaStream_t st) {
+  k_pad_reflect<<<grid_for((size_t)B * c * hp * wp, 256), 256, 0, st>>>(x, y, B, c, h, w, hp, wp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_conv3_small(const float* in, const float* wgt, const float* bias, int B, int H,
+                               int W, int co_n, int act, float slope, float* o32, int ld32,
+                               __half* o16, int ld16, cudaStream_t st) {
+  if (co_n > 256) return cudaErrorInvalidValue;
+  k_conv3_small<<<grid_for((size_t)B * H * W * co_n, 256), 256, 0, st>>>(
+      in, wgt, bias, B, H, W, co_n, act, slope, o32, ld32, o16, ld16);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_zero_cols_f16(__half* x, size_t rows, int c0, int ld, cudaStream_t st) {
+  if (c0 >= ld) return cudaSuccess;
+  k_zero_cols_f16<<<grid_for(rows * (ld - c0), 256), 256, 0, st>>>(x, rows, c0, ld);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bicubic(const float* in, float* out, int BC, int h, int w, int oh, int ow,
+                           cudaStream_t st) {
+  k_bicubic<<<grid_for((size_t)BC * oh * ow, 256), 256, 0, st>>>(in, out, BC, h, w, oh, ow);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_up2_nhwc(const __half* in, __half* out, int B, int H, int W, int C,
+                            cudaStream_t st) {
+  if (C % 8) return cudaErrorInvalidValue;
+  k_up2_nhwc<<<grid_for((size_t)B * 4 * H * W * (C / 8), 256), 256, 0, st>>>(in, out, B, H, W, C);
+  return cudaGetLastError();
+}
+
+}  // namespace s2s

@@ -1,0 +1,147 @@
+"""Host-side logic (no GPU): geometry, weights, conversion, FLOP accounting, and the
+C ABI library's exports."""
+import ctypes
+import subprocess
+
+import numpy as np
+import pytest
+
+from s2s_testlib import ROOT, pkg
+
+
+def test_plan_pads_to_next_window_multiple():
+    P = pkg()
+    # src/plan.rs:39-47: an exact multiple still gains a whole window.
+    pl = P.plan.Plan.new(1080, 1920, 8, 180)
+    assert (pl.hp, pl.wp) == (1088, 1928)
+    pl = P.plan.Plan.new(240, 320, 8, 180)
+    assert (pl.hp, pl.wp, pl.nw, pl.tokens()) == (248, 328, 31 * 41, 81344)
+
+
+def test_plan_index_and_region_follow_the_rolled_plane():
+    P = pkg()
+    pl = P.plan.Plan.new(16, 24, 8, 1)          # 24 x 32 plane, 3 x 4 windows
+    # shifted block: token (0,0) of window 0 reads (4, 4)
+    assert pl.index(0, 0, 4) == (4, 4)
+    # the last window row wraps to image row 0..3
+    assert pl.index(2 * pl.nww, 7 * 8, 4)[0] == (16 + 7 + 4) % 24
+    # regions on the unwrapped coordinate (src/plan.rs:84-108)
+    assert pl.region(0, 0, 4) == (0, 0)
+    last = pl.nw - 1
+    assert pl.region(last, 63, 4) == (2, 2)
+    assert pl.region(last, 0, 4) == (1, 1)
+    # token_pixels is the vectorised index()
+    tp = pl.token_pixels(4)
+    for wi, t in [(0, 0), (5, 17), (last, 63)]:
+        y, x = pl.index(wi, t, 4)
+        assert tp[wi * 64 + t] == y * pl.wp + x
+    assert sorted(tp.tolist()) == list(range(pl.plane()))
+
+
+def test_too_small_image_is_refused():
+    P = pkg()
+    with pytest.raises(ValueError, match="smaller than one 8x8 window"):
+        P.plan.check_size(7, 64, 8)
+
+
+def test_seeded_weights_are_deterministic_and_validated():
+    P = pkg()
+    a = P.weights.Weights.seeded("lightweight_sr", 0)
+    b = P.weights.Weights.seeded("lightweight_sr", 0)
+    for k in a.tensors:
+        assert np.array_equal(a.t(k), b.t(k)), k
+    assert a.upsampler == "pixelshuffledirect" and a.depths == [6, 6, 6, 6]
+    assert a.t("layers.0.residual_group.blocks.0.attn.cpb_pre").shape == (4096, 6)
+    # linear init is normal(0, .02) clamped to two std
+    w = a.t("layers.0.residual_group.blocks.0.mlp.fc1.weight")
+    assert np.abs(w).max() <= 0.04 + 1e-7 and 0.015 < w.std() < 0.02
+
+
+def test_convert_slices_qkv_and_builds_cpb_table():
+    P = pkg()
+    sd = P.weights.seeded_state_dict("lightweight_sr", 3, perturb=True)
+    t, meta = P.weights.convert(sd, "lightweight_sr")
+    p = "layers.1.residual_group.blocks.2.attn"
+    q = sd[f"{p}.qkv.weight"]
+    assert np.array_equal(t[f"{p}.qkv.wk"], q[60:120])
+    assert meta["upsampler"] == "pixelshuffledirect" and meta["depths"] == "6,6,6,6"
+    cpb = t[f"{p}.cpb_pre"]
+    assert cpb.shape == (4096, 6) and cpb.min() > 0 and cpb.max() < 16
+
+
+def test_safetensors_roundtrip_and_tamper(tmp_path):
+    P = pkg()
+    wt = P.weights.Weights.seeded("lightweight_sr", 0)
+    path = tmp_path / "lw.safetensors"
+    P.weights.save_safetensors(path, wt.tensors, wt.meta)
+    back = P.weights.Weights.load(path)
+    assert back.depths == wt.depths
+    for k in wt.tensors:
+        assert np.array_equal(back.t(k), wt.t(k))
+    # a header promising a missing stage is refused, naming the tensor
+    # (tests/parity.rs:198-224 of the reference)
+    meta = dict(wt.meta, depths="6,6,6,6,6")
+    with pytest.raises(ValueError, match="layers.4.residual_group.blocks.0"):
+        P.weights.Weights(wt.tensors, meta)
+
+
+def test_flops_match_the_algorithmic_accounting():
+    P = pkg()
+    wt = P.weights.Weights.seeded("classical_sr", 0)
+    f = wt.flops_forward(248, 328)
+    assert abs(f / 1e9 - 2164) < 2            # 2 164 GFLOP for classical-x4 240x320
+    lw = P.weights.Weights.seeded("lightweight_sr", 0)
+    assert abs(lw.flops_forward(72, 72) / 1e9 - 11.0) < 0.1
+
+
+def _lib_path():
+    import importlib
+    pkg()
+    capi = importlib.import_module("swin2sr_b200.capi")
+    if not capi.LIB_PATH.exists():
+        importlib.import_module("swin2sr_b200.build").build()
+    return capi.LIB_PATH
+
+
+def test_c_abi_library_exports_every_declared_symbol():
+    import importlib
+    P = pkg()
+    capi = importlib.import_module("swin2sr_b200.capi")
+    path = _lib_path()
+    header = (ROOT / "include" / "s2s.h").read_text()
+    import re
+    declared = set(re.findall(r"\b(s2s_[a-z_]+)\s*\(", header))
+    assert declared == set(capi.EXPORTS), declared ^ set(capi.EXPORTS)
+    lib = ctypes.CDLL(str(path))            # loads without a GPU: no CUDA call at load time
+    for sym in declared:
+        assert hasattr(lib, sym), sym
+    lib.s2s_version.restype = ctypes.c_char_p
+    assert b"sm_100a" in lib.s2s_version()
+    nm = subprocess.run(["nm", "-D", "--defined-only", str(path)], capture_output=True,
+                        text=True).stdout
+    for sym in declared:
+        assert f" T {sym}" in nm, sym
+
+
+def test_library_refuses_bad_config_without_touching_the_device():
+    import importlib
+    capi = importlib.import_module("swin2sr_b200.capi")
+    _lib_path()
+    L = capi.load()
+    cfg = capi.S2SConfig()
+    cfg.window = 7                           # unsupported: rejected before any CUDA call
+    h = ctypes.c_void_p()
+    rc = L.s2s_create(ctypes.byref(cfg), None, 0, 0, ctypes.byref(h))
+    assert rc == capi.S2S_ERR_UNSUPPORTED and not h.value
+    assert b"unsupported" in L.s2s_last_error(None)
+
+
+def test_workloads_are_seeded_and_in_range():
+    import importlib
+    wl = importlib.import_module("swin2sr_b200.workloads")
+    a = wl.make_input("classical-x4")
+    b = wl.make_input("classical-x4")
+    assert a.shape == (1, 3, 240, 320) and np.array_equal(a, b)
+    assert 0.0 <= a.min() and a.max() <= 1.0 and a.std() > 0.05
+    rw = wl.make_input("realworld-x4")
+    assert rw.shape == (1, 3, 512, 512) and 0.0 <= rw.min() and rw.max() <= 1.0
