@@ -298,7 +298,7 @@ def main():
 
     def e2e_step():
         np.subtract(x, mean, out=pin_in)          # Pre::adjust on the host
-        pin_in *= np.float32(wt.img_range)
+        np.multiply(pin_in, np.float32(wt.img_range), out=pin_in)
         handle._check(handle.L.s2s_forward_batch(handle.h, B, h, w, capi._fp(pin_in),
                                                  capi._fp(pin_out), None))
 
