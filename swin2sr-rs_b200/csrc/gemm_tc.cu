@@ -1,15 +1,17 @@
 // tcgen05 GEMM and implicit-GEMM 3x3 convolution for sm_100a.
 //
-// One CTA computes a 128 x BN tile of D = A * B^T in TMEM (fp16 operands, fp32
-// accumulation) and runs a fused epilogue on it:
+// A persistent kernel: each CTA owns one N tile and walks M tiles t = blockIdx.x,
+// blockIdx.x + gridDim.x, ... computing 128 x BN tiles of D = A * B^T in TMEM (fp16
+// operands, fp32 accumulation) with a fused epilogue:
 //   warp 0       TMA producer: A and B K-slices (64 fp16 = one 128-byte swizzle row)
-//                into a STAGES-deep shared-memory ring;
-//   warp 1       allocates TMEM, issues tcgen05.mma (K = 16 per instruction) and
-//                frees ring slots with tcgen05.commit;
+//                into a STAGES-deep shared-memory ring that runs across tiles;
+//   warp 1       allocates TMEM, issues tcgen05.mma (K = 16 per instruction), frees
+//                ring slots with tcgen05.commit, and alternates between two TMEM
+//                accumulators so the next tile's MMAs overlap this tile's epilogue;
 //   warps 2..5   epilogue: tcgen05.ld of the accumulator (thread = tile row),
 //                bias / activation / LayerNorm / residual in fp32, then a
-//                shared-memory transpose so that every global store of a warp is
-//                one contiguous row segment.
+//                shared-memory transpose so that every global access of a warp is
+//                four 128-byte row segments (float4 per lane).
 //
 // In conv mode the A tile is a boxh x boxw patch of output pixels and each K-slice
 // is one (tap, 64-channel chunk) of the NHWC input, fetched by a 4-D TMA box at
@@ -23,24 +25,14 @@ namespace s2s {
 namespace {
 
 constexpr int kThreads = 192;
-constexpr int kStageFloats = 32 * 33;  // per epilogue warp: 32 rows x 32 cols, padded
+constexpr int kStageFloats = 32 * 36;  // per epilogue warp: 32 rows x 32 cols, 16-B rows
 
 template <int BN>
 struct TmemCols {
   static constexpr uint32_t value = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
 };
 
-__device__ __forceinline__ float apply_pre(const Epi& e, float v, int col) {
-  if (e.bias) v += e.bias[col];
-  if (e.act == ACT_GELU) {
-    v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
-  } else if (e.act == ACT_LRELU) {
-    v = v < 0.0f ? v * e.slope : v;
-  }
-  return v;
-}
-
-template <int BN, int STAGES>
+template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
            const GemmArgs a) {
@@ -52,28 +44,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   float* stage = reinterpret_cast<float*>(sB + STAGES * B_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(stage + 4 * kStageFloats);
+  float* s_vec = stage + 4 * kStageFloats;                  // bias, LN gamma, LN beta [3][BN]
+  int* s_row = reinterpret_cast<int*>(s_vec + 3 * BN);      // per tile row: src, dst32, dst16, dst32b
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_row + 128 * 4);
   uint64_t* empty = full + STAGES;
-  uint64_t* accf = empty + STAGES;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* accf = empty + STAGES;   // [2] accumulator ready
+  uint64_t* acce = accf + 2;         // [2] accumulator drained
+  uint64_t* fin = acce + 2;          // all MMAs of this CTA retired
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(fin + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr uint32_t NCOLS = TmemCols<BN>::value;
+  constexpr uint32_t NCOLS = TmemCols<2 * BN>::value;
 
-  // Tile coordinates.
-  const int n0 = blockIdx.y * BN;
-  int m0 = 0, bimg = 0, x0 = 0, y0 = 0;
-  if (!a.conv) {
-    m0 = blockIdx.x * 128;
-  } else {
-    const int per_img = a.tiles_x * a.tiles_y;
-    bimg = blockIdx.x / per_img;
-    const int rem = blockIdx.x - bimg * per_img;
-    y0 = (rem / a.tiles_x) * a.boxh;
-    x0 = (rem % a.tiles_x) * a.boxw;
-  }
+  const int NT = a.N / BN;
+  const int tiles_m = a.conv ? a.B * a.tiles_x * a.tiles_y : (a.M + 127) / 128;
+  const int num_tiles = tiles_m * NT;
+  const int G = gridDim.x;  // a multiple of NT: the CTA's N tile is fixed
+  const int n0 = (blockIdx.x % NT) * BN;
   const int num_k = a.conv ? 9 * a.kc : a.K / 64;
+  auto coords = [&](int t, int& m0, int& bimg, int& y0, int& x0) {
+    const int mt = t / NT;
+    m0 = 0;
+    bimg = 0;
+    y0 = 0;
+    x0 = 0;
+    if (!a.conv) {
+      m0 = mt * 128;
+    } else {
+      const int per_img = a.tiles_x * a.tiles_y;
+      bimg = mt / per_img;
+      const int rem = mt - bimg * per_img;
+      y0 = (rem / a.tiles_x) * a.boxh;
+      x0 = (rem % a.tiles_x) * a.boxw;
+    }
+  };
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&mapA);
@@ -82,7 +87,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accf, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    mbar_init(fin, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -97,51 +106,85 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- producer
-      for (int k = 0; k < num_k; k++) {
-        const int s = k % STAGES;
-        if (k >= STAGES) {
-          if (!mbar_wait(&empty[s], ((k / STAGES) - 1) & 1, DEV_TIMEOUT_EMPTY)) break;
+      uint32_t kit = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += G) {
+        int m0, bimg, y0, x0;
+        coords(t, m0, bimg, y0, x0);
+        for (int k = 0; k < num_k; k++, kit++) {
+          const int s = kit % STAGES;
+          if (kit >= STAGES &&
+              !mbar_wait(&empty[s], ((kit / STAGES) - 1) & 1, DEV_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+          if (!a.conv) {
+            tma_load_2d(sA + s * A_BYTES, &mapA, &full[s], k * 64, m0);
+          } else {
+            const int tap = k / a.kc, cc = k - tap * a.kc;
+            const int ky = tap / 3, kx = tap - ky * 3;
+            tma_load_4d(sA + s * A_BYTES, &mapA, &full[s], cc * 64, x0 + kx - 1, y0 + ky - 1,
+                        bimg);
+          }
+          tma_load_2d(sB + s * B_BYTES, &mapB, &full[s], k * 64, n0);
         }
-        mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
-        if (!a.conv) {
-          tma_load_2d(sA + s * A_BYTES, &mapA, &full[s], k * 64, m0);
-        } else {
-          const int tap = k / a.kc, cc = k - tap * a.kc;
-          const int ky = tap / 3, kx = tap - ky * 3;
-          tma_load_4d(sA + s * A_BYTES, &mapA, &full[s], cc * 64, x0 + kx - 1, y0 + ky - 1, bimg);
-        }
-        tma_load_2d(sB + s * B_BYTES, &mapB, &full[s], k * 64, n0);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc = idesc_f16_f32(128, BN);
+      uint32_t kit = 0;
       bool ok = true;
-      for (int k = 0; k < num_k; k++) {
-        const int s = k % STAGES;
-        if (!mbar_wait(&full[s], (k / STAGES) & 1, DEV_TIMEOUT_FULL)) {
-          ok = false;
-          break;
-        }
+      int i = 0;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += G, i++) {
+        const int b = i & 1;
+        if (i >= 2 && !mbar_wait(&acce[b], ((i >> 1) - 1) & 1, DEV_TIMEOUT_ACC)) break;
         tc_fence_after();
-        const uint64_t ad = sw128_desc(smem_u32(sA + s * A_BYTES));
-        const uint64_t bd = sw128_desc(smem_u32(sB + s * B_BYTES));
+        const uint32_t d = tmem + (uint32_t)(b * BN);
+        for (int k = 0; k < num_k; k++, kit++) {
+          const int s = kit % STAGES;
+          if (!mbar_wait(&full[s], (kit / STAGES) & 1, DEV_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(smem_u32(sA + s * A_BYTES));
+          const uint64_t bd = sw128_desc(smem_u32(sB + s * B_BYTES));
 #pragma unroll
-        for (int kk = 0; kk < 4; kk++) {
-          tc_mma_f16(tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                     (k | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; kk++) {
+            tc_mma_f16(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                       (k | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
         }
-        tc_commit(&empty[s]);
+        tc_commit(&accf[b]);
       }
-      (void)ok;
-      tc_commit(accf);
+      // Every MMA this thread issued has retired before TMEM is released.
+      tc_commit(fin);
+      mbar_wait(fin, 0, DEV_TIMEOUT_ACC);
     }
   } else {
     // ---------------------------------------------------------------- epilogue
     const Epi& e = a.epi;
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
+    const int q = warp & 3;           // TMEM lane quarter this warp may read
+    const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+    const int r = q * 32 + lane;      // tile row owned in the thread-per-row phases
+    // Column vectors of this CTA's (fixed) N tile, loaded once.
+    for (int c = et; c < BN; c += 128) {
+      const int col = n0 + c;
+      s_vec[c] = e.bias ? e.bias[col] : 0.0f;
+      s_vec[BN + c] = (e.ln_n > 0 && col < e.ln_n) ? e.ln_g[col] : 0.0f;
+      s_vec[2 * BN + c] = (e.ln_n > 0 && col < e.ln_n) ? e.ln_b[col] : 0.0f;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    float* stg = stage + (warp - 2) * kStageFloats;
+    int i = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += G, i++) {
+    const int b = i & 1;
+    int m0, bimg, y0, x0;
+    coords(t, m0, bimg, y0, x0);
     int mlog, py = 0, px = 0;
     bool valid;
     if (!a.conv) {
@@ -153,29 +196,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       valid = (py < a.H) && (px < a.W);
       mlog = (bimg * a.H + py) * a.W + px;
     }
-    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
-    float* stg = stage + (warp - 2) * kStageFloats;
-    const bool acc_ok = mbar_wait(accf, 0, DEV_TIMEOUT_ACC);
-    tc_fence_after();
+    {
+      int* rw = s_row + r * 4;
+      if constexpr (STORE == STORE_SHUFFLE2) {
+        rw[0] = valid ? mlog : -1;
+        rw[1] = (bimg * 2 * a.H + 2 * py) * (2 * a.W) + 2 * px;  // (dy, dx) = (0, 0) pixel
+        rw[2] = 0;
+        rw[3] = 0;
+      } else {
+        rw[0] = valid ? mlog : -1;
+        rw[1] = valid ? (e.map32 ? e.map32[mlog] : mlog) : 0;
+        rw[2] = valid ? (e.map16 ? e.map16[mlog] : mlog) : 0;
+        rw[3] = valid ? (e.map32b ? e.map32b[mlog] : mlog) : 0;
+      }
+    }
+    __syncwarp();
 
-    if (acc_ok && (e.store == STORE_ROWS || e.store == STORE_SHUFFLE2)) {
+    const uint32_t tbase = tmem + (uint32_t)(b * BN) + ((uint32_t)(q * 32) << 16);
+    const bool acc_ok = mbar_wait(&accf[b], (i >> 1) & 1, DEV_TIMEOUT_ACC);
+    tc_fence_after();
+    if (!acc_ok) break;
+
+    // The epilogue variant is compile-time: the per-element code below is straight
+    // line. Padded columns need no masking: their weights, bias, residual, gamma and
+    // beta are all zero, so they come out as exact zeros and add nothing to the LN
+    // statistics.
+    auto pre = [&](float v, int cl) {
+      v += s_vec[cl];
+      if constexpr (ACT == ACT_GELU) v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+      if constexpr (ACT == ACT_LRELU) v = v < 0.0f ? v * e.slope : v;
+      return v;
+    };
+    const float* rpre = nullptr;
+    if constexpr (RES == 1) rpre = e.res_pre + (size_t)(valid ? mlog : 0) * e.ld_res_pre + n0;
+
+    if constexpr (STORE == STORE_ROWS || STORE == STORE_SHUFFLE2) {
       float mean = 0.0f, rstd = 1.0f;
-      if (e.ln_n > 0) {
+      if constexpr (LN) {
         float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; c++) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
-          const int col0 = n0 + c * 32;
 #pragma unroll
           for (int j = 0; j < 32; j++) {
-            const int col = col0 + j;
-            float x = apply_pre(e, v[j], col);
-            if (e.res_pre && valid) x += e.res_pre[(size_t)mlog * e.ld_res_pre + col];
-            if (col < e.ln_n) {
-              s1 += x;
-              s2 += x * x;
-            }
+            float x = pre(v[j], c * 32 + j);
+            if constexpr (RES == 1) x += rpre[c * 32 + j];
+            s1 += x;
+            s2 += x * x;
           }
         }
         const float nf = (float)e.ln_n;
@@ -183,82 +251,141 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float var = fmaxf(s2 / nf - mean * mean, 0.0f);
         rstd = 1.0f / sqrtf(var + e.ln_eps);
       }
+      const int sub = lane >> 3, cg = lane & 7;  // coalesced phase: 4 rows x 8 lanes
+      const int wrow0 = q * 32;
       const int F = a.N / 4;  // STORE_SHUFFLE2: output channels
 #pragma unroll 1
       for (int c = 0; c < BN / 32; c++) {
         float v[32];
         tmem_ld32(tbase + c * 32, v);
-        const int col0 = n0 + c * 32;
+        const int cl0 = c * 32;
 #pragma unroll
         for (int j = 0; j < 32; j++) {
-          const int col = col0 + j;
-          float x = apply_pre(e, v[j], col);
-          if (e.res_pre && valid) x += e.res_pre[(size_t)mlog * e.ld_res_pre + col];
-          if (e.ln_n > 0) x = col < e.ln_n ? (x - mean) * rstd * e.ln_g[col] + e.ln_b[col] : 0.0f;
-          if (col >= e.n_valid) x = 0.0f;
-          stg[lane * 33 + j] = x;
+          float x = pre(v[j], cl0 + j);
+          if constexpr (RES == 1) x += rpre[cl0 + j];
+          if constexpr (LN) x = (x - mean) * rstd * s_vec[BN + cl0 + j] + s_vec[2 * BN + cl0 + j];
+          v[j] = x;
         }
+        float4* srow = reinterpret_cast<float4*>(stg + lane * 36);
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          srow[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         __syncwarp();
-        const int col = col0 + lane;
-#pragma unroll 1
-        for (int rr = 0; rr < 32; rr++) {
-          const int m2 = __shfl_sync(0xffffffffu, mlog, rr);
-          const int ok2 = __shfl_sync(0xffffffffu, (int)valid, rr);
-          const int py2 = __shfl_sync(0xffffffffu, py, rr);
-          const int px2 = __shfl_sync(0xffffffffu, px, rr);
-          if (!ok2) continue;
-          float x = stg[rr * 33 + lane];
-          if (e.store == STORE_ROWS) {
-            if (e.res_post) x += e.res_post[(size_t)m2 * e.ld_res_post + col];
-            if (e.o32) e.o32[(size_t)(e.map32 ? e.map32[m2] : m2) * e.ld32 + col] = x;
-            if (e.o32b) e.o32b[(size_t)(e.map32b ? e.map32b[m2] : m2) * e.ld32b + col] = x;
-            if (e.o16)
-              e.o16[(size_t)(e.map16 ? e.map16[m2] : m2) * e.ld16 + col] = __float2half_rn(x);
-          } else {
-            const int qd = col / F, f = col - qd * F;
-            const int dy = qd >> 1, dx = qd & 1;
-            const size_t dst =
-                ((size_t)(bimg * 2 * a.H + 2 * py2 + dy) * (2 * a.W) + (2 * px2 + dx)) * F + f;
-            if (e.res_post) x += e.res_post[dst];
-            e.o16[dst] = __float2half_rn(x);
+        const int col = n0 + cl0 + cg * 4;
+        float4 val[8];
+        int src[8];
+#pragma unroll
+        for (int it = 0; it < 8; it++) {
+          const int rr = it * 4 + sub;
+          val[it] = *reinterpret_cast<const float4*>(stg + rr * 36 + cg * 4);
+          src[it] = s_row[(wrow0 + rr) * 4];
+        }
+        if constexpr (STORE == STORE_ROWS) {
+          if constexpr (RES == 2) {
+            float4 rp[8];
+#pragma unroll
+            for (int it = 0; it < 8; it++)
+              rp[it] = src[it] >= 0 ? __ldg(reinterpret_cast<const float4*>(
+                                          e.res_post + (size_t)src[it] * e.ld_res_post + col))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+              val[it].x += rp[it].x;
+              val[it].y += rp[it].y;
+              val[it].z += rp[it].z;
+              val[it].w += rp[it].w;
+            }
+          }
+#pragma unroll
+          for (int it = 0; it < 8; it++) {
+            if (src[it] < 0) continue;
+            const int4 rw = *reinterpret_cast<const int4*>(s_row + (wrow0 + it * 4 + sub) * 4);
+            if (e.o32) *reinterpret_cast<float4*>(e.o32 + (size_t)rw.y * e.ld32 + col) = val[it];
+            if (e.o32b)
+              *reinterpret_cast<float4*>(e.o32b + (size_t)rw.w * e.ld32b + col) = val[it];
+            if (e.o16) {
+              __half2 h0 = __floats2half2_rn(val[it].x, val[it].y);
+              __half2 h1 = __floats2half2_rn(val[it].z, val[it].w);
+              uint2 u;
+              u.x = *reinterpret_cast<uint32_t*>(&h0);
+              u.y = *reinterpret_cast<uint32_t*>(&h1);
+              *reinterpret_cast<uint2*>(e.o16 + (size_t)rw.z * e.ld16 + col) = u;
+            }
+          }
+        } else {
+          const int qd = col / F, f = col - qd * F;
+          const int dy = qd >> 1, dx = qd & 1;
+          size_t dst[8];
+#pragma unroll
+          for (int it = 0; it < 8; it++)
+            dst[it] = ((size_t)s_row[(wrow0 + it * 4 + sub) * 4 + 1] + (size_t)dy * (2 * a.W) + dx) *
+                          F + f;
+          if constexpr (RES == 2) {
+            float4 rp[8];
+#pragma unroll
+            for (int it = 0; it < 8; it++)
+              rp[it] = src[it] >= 0 ? __ldg(reinterpret_cast<const float4*>(e.res_post + dst[it]))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+              val[it].x += rp[it].x;
+              val[it].y += rp[it].y;
+              val[it].z += rp[it].z;
+              val[it].w += rp[it].w;
+            }
+          }
+#pragma unroll
+          for (int it = 0; it < 8; it++) {
+            if (src[it] < 0) continue;
+            __half2 h0 = __floats2half2_rn(val[it].x, val[it].y);
+            __half2 h1 = __floats2half2_rn(val[it].z, val[it].w);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t*>(&h0);
+            u.y = *reinterpret_cast<uint32_t*>(&h1);
+            *reinterpret_cast<uint2*>(e.o16 + dst[it]) = u;
           }
         }
         __syncwarp();
       }
-    } else if (acc_ok && e.store == STORE_PLANES) {
+    } else if constexpr (STORE == STORE_PLANES) {
       float v[32];
       tmem_ld32(tbase, v);
       if (valid) {
-        const float mean[3] = {e.mean0, e.mean1, e.mean2};
 #pragma unroll
         for (int ch = 0; ch < 3; ch++) {
-          const float x = apply_pre(e, v[ch], ch);
+          const float x = pre(v[ch], ch);
+          const float mean = ch == 0 ? e.mean0 : ch == 1 ? e.mean1 : e.mean2;
           if (e.planes_raw)
             e.planes_raw[((size_t)(bimg * 3 + ch) * a.H + py) * a.W + px] = x;
           if (e.planes && py < e.crop_h && px < e.crop_w)
             e.planes[((size_t)(bimg * 3 + ch) * e.crop_h + py) * e.crop_w + px] =
-                x / e.img_range + mean[ch];
+                x / e.img_range + mean;
         }
       }
-    } else if (acc_ok && e.store == STORE_DIRECT) {
-      const float mean[3] = {e.mean0, e.mean1, e.mean2};
+    } else {  // STORE_DIRECT
       const int s = e.scale, s2 = s * s, nout = 3 * s2;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; c++) {
         float v[32];
         tmem_ld32(tbase + c * 32, v);
-        if (!valid) continue;
-#pragma unroll 4
+#pragma unroll
         for (int j = 0; j < 32; j++) {
           const int col = c * 32 + j;
-          if (col >= nout) break;
+          if (!valid || col >= nout) continue;
           const int ch = col / s2, rem = col - ch * s2, dy = rem / s, dx = rem - dy * s;
           const int Y = py * s + dy, X = px * s + dx;
+          const float mean = ch == 0 ? e.mean0 : ch == 1 ? e.mean1 : e.mean2;
           if (Y < e.crop_h && X < e.crop_w)
             e.planes[((size_t)(bimg * 3 + ch) * e.crop_h + Y) * e.crop_w + X] =
-                apply_pre(e, v[j], col) / e.img_range + mean[ch];
+                pre(v[j], col) / e.img_range + mean;
         }
       }
+    }
+
+    // Release this accumulator buffer to the MMA warp.
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&acce[b]);
     }
   }
 
@@ -270,43 +397,79 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE>
 cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& a,
                      cudaStream_t st) {
   const size_t smem = 1024 + (size_t)STAGES * (128 * 128 + BN * 128) + 4 * kStageFloats * 4 +
-                      (2 * STAGES + 1) * 8 + 16;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t err = cudaFuncSetAttribute(k_gemm<BN, STAGES>,
+                      3 * BN * 4 + 128 * 4 * 4 + (2 * STAGES + 5) * 8 + 16;
+  static int ctas = 0;  // resident CTAs per device (SMs x CTAs per SM), one process per GPU
+  if (ctas == 0) {
+    cudaError_t err = cudaFuncSetAttribute(k_gemm<BN, STAGES, ACT, LN, RES, STORE>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
-    attr_set = true;
+    int dev = 0, sms = 0, occ = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_gemm<BN, STAGES, ACT, LN, RES, STORE>, kThreads, smem);
+    if (err != cudaSuccess) return err;
+    if (occ < 1) return cudaErrorInvalidConfiguration;
+    ctas = sms * occ;
   }
-  dim3 grid;
-  if (a.conv)
-    grid = dim3((unsigned)(a.B * a.tiles_x * a.tiles_y), (unsigned)(a.N / BN));
-  else
-    grid = dim3((unsigned)((a.M + 127) / 128), (unsigned)(a.N / BN));
-  k_gemm<BN, STAGES><<<grid, kThreads, smem, st>>>(mapA, mapB, a);
+  const int NT = a.N / BN;
+  const int tiles_m = a.conv ? a.B * a.tiles_x * a.tiles_y : (a.M + 127) / 128;
+  const long tiles = (long)tiles_m * NT;
+  long G = tiles < ctas ? tiles : ctas;
+  G = (G / NT) * NT;
+  if (G < NT) G = NT;
+  k_gemm<BN, STAGES, ACT, LN, RES, STORE><<<(unsigned)G, kThreads, smem, st>>>(mapA, mapB, a);
   return cudaGetLastError();
 }
 
 }  // namespace
 
+// The epilogue variants the forward pass uses, per N tile.
+#define S2S_VARIANT(BN_, ST_, ACT_, LN_, RES_, STORE_)                                 \
+  if (BN == BN_ && act == ACT_ && ln == LN_ && res == RES_ && store == STORE_)        \
+    return launch_t<BN_, ST_, ACT_, LN_, RES_, STORE_>(mapA, mapB, a, st);
+
 cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& a,
                         int BN, cudaStream_t st) {
   if (a.N % BN != 0 || (a.conv == 0 && a.K % 64 != 0)) return cudaErrorInvalidValue;
-  if (a.epi.ln_n > 0 && a.N != BN) return cudaErrorInvalidValue;
-  switch (BN) {
-    case 32: return launch_t<32, 4>(mapA, mapB, a, st);
-    case 64: return launch_t<64, 4>(mapA, mapB, a, st);
-    case 96: return launch_t<96, 3>(mapA, mapB, a, st);
-    case 128: return launch_t<128, 3>(mapA, mapB, a, st);
-    case 192: return launch_t<192, 2>(mapA, mapB, a, st);
-    case 256: return launch_t<256, 2>(mapA, mapB, a, st);
-    default: return cudaErrorInvalidValue;
-  }
+  const Epi& e = a.epi;
+  if (e.ln_n > 0 && a.N != BN) return cudaErrorInvalidValue;
+  if (e.res_pre && e.res_post) return cudaErrorInvalidValue;
+  const int act = e.act;
+  const bool ln = e.ln_n > 0;
+  const int res = e.res_pre ? 1 : (e.res_post ? 2 : 0);
+  const int store = e.store;
+  // embed 180 (Cp 192): QKV, convs, fc1, proj/fc2, patch_embed, stage tail, body skip
+  S2S_VARIANT(192, 4, ACT_NONE, false, 0, STORE_ROWS)
+  S2S_VARIANT(192, 4, ACT_GELU, false, 0, STORE_ROWS)
+  S2S_VARIANT(192, 4, ACT_NONE, true, 2, STORE_ROWS)
+  S2S_VARIANT(192, 4, ACT_NONE, true, 0, STORE_ROWS)
+  S2S_VARIANT(192, 4, ACT_NONE, false, 1, STORE_ROWS)
+  S2S_VARIANT(192, 4, ACT_NONE, true, 1, STORE_ROWS)
+  S2S_VARIANT(192, 4, ACT_NONE, false, 2, STORE_ROWS)
+  // embed 60 (Cp 64) and the 64-channel head convs
+  S2S_VARIANT(64, 6, ACT_NONE, false, 0, STORE_ROWS)
+  S2S_VARIANT(64, 6, ACT_NONE, true, 2, STORE_ROWS)
+  S2S_VARIANT(64, 6, ACT_NONE, true, 0, STORE_ROWS)
+  S2S_VARIANT(64, 6, ACT_NONE, false, 1, STORE_ROWS)
+  S2S_VARIANT(64, 6, ACT_NONE, true, 1, STORE_ROWS)
+  S2S_VARIANT(64, 6, ACT_NONE, false, 2, STORE_ROWS)
+  S2S_VARIANT(64, 6, ACT_LRELU, false, 0, STORE_ROWS)
+  S2S_VARIANT(96, 6, ACT_NONE, false, 0, STORE_ROWS)
+  S2S_VARIANT(128, 4, ACT_GELU, false, 0, STORE_ROWS)
+  // x2 octave convs with the pixel-shuffle store (+ the compressed head's bicubic add)
+  S2S_VARIANT(256, 4, ACT_NONE, false, 0, STORE_SHUFFLE2)
+  S2S_VARIANT(256, 4, ACT_NONE, false, 2, STORE_SHUFFLE2)
+  // 3-channel outputs
+  S2S_VARIANT(32, 6, ACT_NONE, false, 0, STORE_PLANES)
+  S2S_VARIANT(32, 6, ACT_NONE, false, 0, STORE_DIRECT)
+  S2S_VARIANT(64, 6, ACT_NONE, false, 0, STORE_DIRECT)
+  return cudaErrorNotSupported;
 }
+#undef S2S_VARIANT
 
 // ------------------------------------------------------------------- TMA maps
 namespace {
