@@ -1,10 +1,11 @@
 // SwinV2 scaled-cosine window attention (reference: src/cpu.rs:1244-1402,
 // tools/network_swin2sr.py:151-190).
 //
-// One CTA per 8x8 window; four warps, each owning 16 query rows, loop over the
-// heads. Per head:
+// One CTA per 8x8 window, eight warps. The reciprocal L2 norms of every q and k
+// row of every head are computed once per window; then each warp takes (head,
+// 16-query-row block) tasks independently. Per task:
 //   S = Q K^T          mma.sync m16n8k16 fp16 -> fp32 (16 x 64 per warp, in registers)
-//   s = S / (|q| |k|) * exp(min(logit_scale, ln 100)) + cpb[h][q][k]  (- 100 across shift
+//   s = S * (1/|q|) * (1/|k|) * exp(min(logit_scale, ln 100)) + cpb[h][q][k]  (- 100 across shift
 //       regions; the region of a token is computed from its rolled plane coordinate)
 //   softmax along the row in registers (quad shuffles), max-subtracted
 //   O = P V            mma.sync, P re-used from the S accumulators as fp16 A fragments
@@ -60,7 +61,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 // DP: padded head dim (16 or 32). Window of 64 tokens (win = 8).
 template <int DP>
-__global__ void __launch_bounds__(128) k_window_attention(
+__global__ void __launch_bounds__(256) k_window_attention(
     const __half* __restrict__ qkv, __half* __restrict__ out, const float* __restrict__ cpb,
     const float* __restrict__ lscale, int heads, int hd, int ld_out, int nwh, int nww, int hp,
     int wp, int shift) {
@@ -70,8 +71,9 @@ __global__ void __launch_bounds__(128) k_window_attention(
   const int sstride = row_h + 8;               // padded smem row (halves): odd number of 16 B
   extern __shared__ uint8_t smem_raw[];
   __half* sq = reinterpret_cast<__half*>(smem_raw);
-  float* snorm = reinterpret_cast<float*>(smem_raw + (size_t)N * sstride * 2);  // [2][64]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(snorm + 2 * N);
+  // [heads][2][64]: 1/|k| then 1/|q| per head
+  float* snorm = reinterpret_cast<float*>(smem_raw + (size_t)N * sstride * 2);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(snorm + 2 * N * heads);
 
   const int win_idx = blockIdx.x;              // global window (image-major)
   const int nw = nwh * nww;
@@ -92,40 +94,30 @@ __global__ void __launch_bounds__(128) k_window_attention(
   const bool ok = mbar_wait(bar, 0, DEV_TIMEOUT_FULL);
   if (!__syncthreads_and(ok)) return;  // uniform exit: no thread is left at a barrier
 
-  // Query rows of this thread (within the window) and their shift regions.
-  const int qr0 = warp * 16 + g, qr1 = qr0 + 8;
-  int qreg0 = 0, qreg1 = 0;
-  if (shift) {
-    qreg0 = 3 * region_of(wh * 8 + qr0 / 8, hp, 8, shift) + region_of(ww * 8 + qr0 % 8, wp, 8, shift);
-    qreg1 = 3 * region_of(wh * 8 + qr1 / 8, hp, 8, shift) + region_of(ww * 8 + qr1 % 8, wp, 8, shift);
-  }
-  int kreg[8][2];
-#pragma unroll
-  for (int j = 0; j < 8; j++)
-#pragma unroll
-    for (int e = 0; e < 2; e++) {
-      const int k = 8 * j + 2 * t4 + e;
-      kreg[j][e] = shift ? 3 * region_of(wh * 8 + k / 8, hp, 8, shift) +
-                               region_of(ww * 8 + k % 8, wp, 8, shift)
-                         : 0;
+  // Reciprocal norms of every head's q and k rows, from the same fp16 values the MMAs read.
+  for (int idx = tid; idx < 2 * N * heads; idx += blockDim.x) {
+    const int h = idx / (2 * N), rem = idx - h * 2 * N;
+    const int isq = rem >= N, tok = rem & (N - 1);
+    const __half* v = sq + (size_t)tok * sstride + (isq ? h : heads + h) * DP;
+    float acc = 0.0f;
+    for (int d = 0; d < hd; d++) {
+      const float x = __half2float(v[d]);
+      acc += x * x;
     }
+    snorm[idx] = 1.0f / fmaxf(sqrtf(acc), 1e-12f);
+  }
+  __syncthreads();
 
   const uint32_t sbase = smem_u32(sq);
-  for (int h = 0; h < heads; h++) {
-    const int qoff = h * DP, koff = (heads + h) * DP, voff = (2 * heads + h) * DP;
-    // |q| and |k| of this head, from the same fp16 values the MMAs read.
-    __syncthreads();
-    {
-      const int tok = tid & 63;
-      const int off = tid < 64 ? koff : qoff;
-      float s = 0.0f;
-      for (int d = 0; d < hd; d++) {
-        const float v = __half2float(sq[(size_t)tok * sstride + off + d]);
-        s += v * v;
-      }
-      snorm[(tid < 64 ? 0 : N) + tok] = fmaxf(sqrtf(s), 1e-12f);
+  for (int task = warp; task < heads * 4; task += 8) {
+    const int h = task >> 2, rb = task & 3;
+    const int qr0 = rb * 16 + g, qr1 = qr0 + 8;
+    int qreg0 = 0, qreg1 = 0;
+    if (shift) {
+      qreg0 = 3 * region_of(wh * 8 + qr0 / 8, hp, 8, shift) + region_of(ww * 8 + qr0 % 8, wp, 8, shift);
+      qreg1 = 3 * region_of(wh * 8 + qr1 / 8, hp, 8, shift) + region_of(ww * 8 + qr1 % 8, wp, 8, shift);
     }
-    __syncthreads();
+    const int qoff = h * DP, koff = (heads + h) * DP, voff = (2 * heads + h) * DP;
 
     // S = Q K^T for 16 rows x 64 keys.
     float sacc[8][4];
@@ -134,7 +126,7 @@ __global__ void __launch_bounds__(128) k_window_attention(
 #pragma unroll
     for (int kk = 0; kk < DP / 16; kk++) {
       uint32_t a0, a1, a2, a3;
-      const int arow = warp * 16 + (lane & 15);
+      const int arow = rb * 16 + (lane & 15);
       const int acol = qoff + kk * 16 + (lane >> 4) * 8;
       ldsm_x4(sbase + (uint32_t)((arow * sstride + acol) * 2), a0, a1, a2, a3);
 #pragma unroll
@@ -150,25 +142,29 @@ __global__ void __launch_bounds__(128) k_window_attention(
 
     // Scale, bias, mask, softmax.
     const float ls = lscale[h];
-    const float qn0 = snorm[N + qr0], qn1 = snorm[N + qr1];
+    const float* kinv = snorm + h * 2 * N;
+    const float qs0 = kinv[N + qr0] * ls, qs1 = kinv[N + qr1] * ls;
     const float* cp0 = cpb + ((size_t)h * N + qr0) * N;
     const float* cp1 = cpb + ((size_t)h * N + qr1) * N;
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       const int k = 8 * j + 2 * t4;
-      const float kn0 = snorm[k], kn1 = snorm[k + 1];
-      const float2 b0 = *reinterpret_cast<const float2*>(cp0 + k);
-      const float2 b1 = *reinterpret_cast<const float2*>(cp1 + k);
-      float s00 = sacc[j][0] / (qn0 * kn0) * ls + b0.x;
-      float s01 = sacc[j][1] / (qn0 * kn1) * ls + b0.y;
-      float s10 = sacc[j][2] / (qn1 * kn0) * ls + b1.x;
-      float s11 = sacc[j][3] / (qn1 * kn1) * ls + b1.y;
+      const float ki0 = kinv[k], ki1 = kinv[k + 1];
+      const float2 b0 = __ldg(reinterpret_cast<const float2*>(cp0 + k));
+      const float2 b1 = __ldg(reinterpret_cast<const float2*>(cp1 + k));
+      float s00 = sacc[j][0] * ki0 * qs0 + b0.x;
+      float s01 = sacc[j][1] * ki1 * qs0 + b0.y;
+      float s10 = sacc[j][2] * ki0 * qs1 + b1.x;
+      float s11 = sacc[j][3] * ki1 * qs1 + b1.y;
       if (shift) {
-        if (qreg0 != kreg[j][0]) s00 -= 100.0f;
-        if (qreg0 != kreg[j][1]) s01 -= 100.0f;
-        if (qreg1 != kreg[j][0]) s10 -= 100.0f;
-        if (qreg1 != kreg[j][1]) s11 -= 100.0f;
+        const int kr0 = 3 * region_of(wh * 8 + k / 8, hp, 8, shift) + region_of(ww * 8 + k % 8, wp, 8, shift);
+        const int kr1 = 3 * region_of(wh * 8 + (k + 1) / 8, hp, 8, shift) +
+                        region_of(ww * 8 + (k + 1) % 8, wp, 8, shift);
+        if (qreg0 != kr0) s00 -= 100.0f;
+        if (qreg0 != kr1) s01 -= 100.0f;
+        if (qreg1 != kr0) s10 -= 100.0f;
+        if (qreg1 != kr1) s11 -= 100.0f;
       }
       sacc[j][0] = s00;
       sacc[j][1] = s01;
@@ -239,7 +235,7 @@ cudaError_t launch_window_attention(const __half* qkv, __half* out, const float*
                                     int dp, int ld_out, int nwh, int nww, int hp, int wp,
                                     int shift, cudaStream_t st) {
   const int row_h = 3 * heads * dp;
-  const size_t smem = (size_t)64 * (row_h + 8) * 2 + 2 * 64 * 4 + 16;
+  const size_t smem = (size_t)64 * (row_h + 8) * 2 + 2 * 64 * heads * 4 + 16;
   if (dp == 32) {
     static bool set = false;
     if (!set) {
@@ -247,7 +243,7 @@ cudaError_t launch_window_attention(const __half* qkv, __half* out, const float*
                            (int)smem);
       set = true;
     }
-    k_window_attention<32><<<nwin_total, 128, smem, st>>>(qkv, out, cpb, lscale, heads, hd,
+    k_window_attention<32><<<nwin_total, 256, smem, st>>>(qkv, out, cpb, lscale, heads, hd,
                                                           ld_out, nwh, nww, hp, wp, shift);
   } else if (dp == 16) {
     static bool set = false;
@@ -256,7 +252,7 @@ cudaError_t launch_window_attention(const __half* qkv, __half* out, const float*
                            (int)smem);
       set = true;
     }
-    k_window_attention<16><<<nwin_total, 128, smem, st>>>(qkv, out, cpb, lscale, heads, hd,
+    k_window_attention<16><<<nwin_total, 256, smem, st>>>(qkv, out, cpb, lscale, heads, hd,
                                                           ld_out, nwh, nww, hp, wp, shift);
   } else {
     return cudaErrorInvalidValue;

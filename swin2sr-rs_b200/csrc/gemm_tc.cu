@@ -8,7 +8,8 @@
 //   warp 1       allocates TMEM, issues tcgen05.mma (K = 16 per instruction), frees
 //                ring slots with tcgen05.commit, and alternates between two TMEM
 //                accumulators so the next tile's MMAs overlap this tile's epilogue;
-//   warps 2..5   epilogue: tcgen05.ld of the accumulator (thread = tile row),
+//   warps 2..9   epilogue, two warps per TMEM lane quarter splitting the columns:
+//                tcgen05.ld of the accumulator (thread = tile row),
 //                bias / activation / LayerNorm / residual in fp32, then a
 //                shared-memory transpose so that every global access of a warp is
 //                four 128-byte row segments (float4 per lane).
@@ -24,7 +25,8 @@ namespace s2s {
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
+constexpr int kEpiWarps = 8;
 constexpr int kStageFloats = 32 * 36;  // per epilogue warp: 32 rows x 32 cols, 16-B rows
 
 template <int BN>
@@ -44,9 +46,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   float* stage = reinterpret_cast<float*>(sB + STAGES * B_BYTES);
-  float* s_vec = stage + 4 * kStageFloats;                  // bias, LN gamma, LN beta [3][BN]
-  int* s_row = reinterpret_cast<int*>(s_vec + 3 * BN);      // per tile row: src, dst32, dst16, dst32b
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_row + 128 * 4);
+  float* s_vec = stage + kEpiWarps * kStageFloats;          // bias, LN gamma, LN beta [3][BN]
+  int* s_rows = reinterpret_cast<int*>(s_vec + 3 * BN);     // per warp, per row: src, dst32, dst16, dst32b
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_rows + kEpiWarps * 32 * 4);
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;   // [2] accumulator ready
   uint64_t* acce = accf + 2;         // [2] accumulator drained
@@ -89,7 +91,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], 4);
+      mbar_init(&acce[b], kEpiWarps);
     }
     mbar_init(fin, 1);
     fence_barrier_init();
@@ -169,16 +171,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- epilogue
     const Epi& e = a.epi;
     const int q = warp & 3;           // TMEM lane quarter this warp may read
-    const int et = threadIdx.x - 64;  // 0..127 among the epilogue threads
+    const int half = (warp - 2) >> 2; // which interleaved half of the column chunks
+    const int et = threadIdx.x - 64;  // 0..255 among the epilogue threads
     const int r = q * 32 + lane;      // tile row owned in the thread-per-row phases
+    int* s_row = s_rows + (warp - 2) * 32 * 4 - q * 32 * 4;  // indexed by tile row q*32..q*32+31
     // Column vectors of this CTA's (fixed) N tile, loaded once.
-    for (int c = et; c < BN; c += 128) {
+    for (int c = et; c < BN; c += 32 * kEpiWarps) {
       const int col = n0 + c;
       s_vec[c] = e.bias ? e.bias[col] : 0.0f;
       s_vec[BN + c] = (e.ln_n > 0 && col < e.ln_n) ? e.ln_g[col] : 0.0f;
       s_vec[2 * BN + c] = (e.ln_n > 0 && col < e.ln_n) ? e.ln_b[col] : 0.0f;
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
     float* stg = stage + (warp - 2) * kStageFloats;
     int i = 0;
     for (int t = blockIdx.x; t < num_tiles; t += G, i++) {
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int wrow0 = q * 32;
       const int F = a.N / 4;  // STORE_SHUFFLE2: output channels
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
+      for (int c = half; c < BN / 32; c += 2) {
         float v[32];
         tmem_ld32(tbase + c * 32, v);
         const int cl0 = c * 32;
@@ -350,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if constexpr (STORE == STORE_PLANES) {
       float v[32];
       tmem_ld32(tbase, v);
-      if (valid) {
+      if (valid && half == 0) {
 #pragma unroll
         for (int ch = 0; ch < 3; ch++) {
           const float x = pre(v[ch], ch);
@@ -365,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {  // STORE_DIRECT
       const int s = e.scale, s2 = s * s, nout = 3 * s2;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; c++) {
+      for (int c = half; c < BN / 32; c += 2) {
         float v[32];
         tmem_ld32(tbase + c * 32, v);
 #pragma unroll
@@ -400,8 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE>
 cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& a,
                      cudaStream_t st) {
-  const size_t smem = 1024 + (size_t)STAGES * (128 * 128 + BN * 128) + 4 * kStageFloats * 4 +
-                      3 * BN * 4 + 128 * 4 * 4 + (2 * STAGES + 5) * 8 + 16;
+  const size_t smem = 1024 + (size_t)STAGES * (128 * 128 + BN * 128) +
+                      kEpiWarps * kStageFloats * 4 + 3 * BN * 4 + kEpiWarps * 32 * 4 * 4 +
+                      (2 * STAGES + 5) * 8 + 16;
   static int ctas = 0;  // resident CTAs per device (SMs x CTAs per SM), one process per GPU
   if (ctas == 0) {
     cudaError_t err = cudaFuncSetAttribute(k_gemm<BN, STAGES, ACT, LN, RES, STORE>,
@@ -461,8 +466,8 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   S2S_VARIANT(96, 6, ACT_NONE, false, 0, STORE_ROWS)
   S2S_VARIANT(128, 4, ACT_GELU, false, 0, STORE_ROWS)
   // x2 octave convs with the pixel-shuffle store (+ the compressed head's bicubic add)
-  S2S_VARIANT(256, 4, ACT_NONE, false, 0, STORE_SHUFFLE2)
-  S2S_VARIANT(256, 4, ACT_NONE, false, 2, STORE_SHUFFLE2)
+  S2S_VARIANT(256, 3, ACT_NONE, false, 0, STORE_SHUFFLE2)
+  S2S_VARIANT(256, 3, ACT_NONE, false, 2, STORE_SHUFFLE2)
   // 3-channel outputs
   S2S_VARIANT(32, 6, ACT_NONE, false, 0, STORE_PLANES)
   S2S_VARIANT(32, 6, ACT_NONE, false, 0, STORE_DIRECT)
