@@ -132,7 +132,7 @@ int64_t s2s_launch_count(const s2s_handle* h);
  * 1453-1459, which name every activation for bisection against the torch
  * network): stop the next forwards after `launches` kernel launches (-1 = run
  * to the end), and read a named workspace buffer of the current plan back as
- * fp32 ("P", "F0", "F0h", "X0", "X1", "X16_0", "X16_1", "S", "QKV", "AO", "H16",
+ * fp32 ("P", "F0", "F0h", "X", "X16", "S", "QKV", "AO", "H16",
  * "HA", "HB0", "HB1", "HB2", "BIC", "BICF", "AUXRAW"). s2s_debug_read returns
  * the element count, or -1 for an unknown name / no plan. */
 int s2s_debug_stop_after(s2s_handle* h, int64_t launches);

@@ -10,9 +10,13 @@
 //   softmax along the row in registers (quad shuffles), max-subtracted
 //   O = P V            mma.sync, P re-used from the S accumulators as fp16 A fragments
 //   out[token][h*hd + d] = O / rowsum
-// The window's q/k/v rows (fp16, [3][heads][DP] per token, pad lanes zero) are
-// brought in with one bulk copy per token row into a padded, bank-conflict-free
-// shared-memory layout.
+// The residual stream and every token-row buffer stay in image order; this kernel
+// is the only place the window partition and cyclic roll exist: `rows` maps the
+// window-major token (b, wi, t) of the block's shift to its image row
+// (src/plan.rs:72-78), so the window's q/k/v rows (fp16, [3][heads][DP] per token,
+// pad lanes zero) are gathered with one bulk copy per token row into a padded,
+// bank-conflict-free shared-memory layout, and outputs are scattered back to the
+// same rows.
 #include "common.cuh"
 
 namespace s2s {
@@ -63,8 +67,8 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 template <int DP>
 __global__ void __launch_bounds__(256) k_window_attention(
     const __half* __restrict__ qkv, __half* __restrict__ out, const float* __restrict__ cpb,
-    const float* __restrict__ lscale, int heads, int hd, int ld_out, int nwh, int nww, int hp,
-    int wp, int shift) {
+    const float* __restrict__ lscale, const int* __restrict__ rows, int heads, int hd, int ld_out,
+    int nwh, int nww, int hp, int wp, int shift) {
   constexpr int N = 64;
   const int row_h = 3 * heads * DP;            // halves per token row
   const int row_bytes = row_h * 2;
@@ -90,7 +94,8 @@ __global__ void __launch_bounds__(256) k_window_attention(
   __syncthreads();
   if (tid == 0) mbar_arrive_expect_tx(bar, (uint32_t)(N * row_bytes));
   __syncthreads();
-  if (tid < N) bulk_g2s(sq + (size_t)tid * sstride, qkv + (tok0 + tid) * row_h, row_bytes, bar);
+  if (tid < N)
+    bulk_g2s(sq + (size_t)tid * sstride, qkv + (size_t)rows[tok0 + tid] * row_h, row_bytes, bar);
   const bool ok = mbar_wait(bar, 0, DEV_TIMEOUT_FULL);
   if (!__syncthreads_and(ok)) return;  // uniform exit: no thread is left at a barrier
 
@@ -213,8 +218,8 @@ __global__ void __launch_bounds__(256) k_window_attention(
       }
     }
     const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
-    __half* o0 = out + (tok0 + qr0) * (size_t)ld_out + h * hd;
-    __half* o1 = out + (tok0 + qr1) * (size_t)ld_out + h * hd;
+    __half* o0 = out + (size_t)rows[tok0 + qr0] * ld_out + h * hd;
+    __half* o1 = out + (size_t)rows[tok0 + qr1] * ld_out + h * hd;
 #pragma unroll
     for (int n = 0; n < DP / 8; n++) {
       const int d = n * 8 + 2 * t4;
@@ -231,9 +236,9 @@ __global__ void __launch_bounds__(256) k_window_attention(
 }  // namespace
 
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
-                                    const float* lscale, int nwin_total, int heads, int hd,
-                                    int dp, int ld_out, int nwh, int nww, int hp, int wp,
-                                    int shift, cudaStream_t st) {
+                                    const float* lscale, const int* rows, int nwin_total,
+                                    int heads, int hd, int dp, int ld_out, int nwh, int nww,
+                                    int hp, int wp, int shift, cudaStream_t st) {
   const int row_h = 3 * heads * dp;
   const size_t smem = (size_t)64 * (row_h + 8) * 2 + 2 * 64 * heads * 4 + 16;
   if (dp == 32) {
@@ -243,7 +248,7 @@ cudaError_t launch_window_attention(const __half* qkv, __half* out, const float*
                            (int)smem);
       set = true;
     }
-    k_window_attention<32><<<nwin_total, 256, smem, st>>>(qkv, out, cpb, lscale, heads, hd,
+    k_window_attention<32><<<nwin_total, 256, smem, st>>>(qkv, out, cpb, lscale, rows, heads, hd,
                                                           ld_out, nwh, nww, hp, wp, shift);
   } else if (dp == 16) {
     static bool set = false;
@@ -252,7 +257,7 @@ cudaError_t launch_window_attention(const __half* qkv, __half* out, const float*
                            (int)smem);
       set = true;
     }
-    k_window_attention<16><<<nwin_total, 256, smem, st>>>(qkv, out, cpb, lscale, heads, hd,
+    k_window_attention<16><<<nwin_total, 256, smem, st>>>(qkv, out, cpb, lscale, rows, heads, hd,
                                                           ld_out, nwh, nww, hp, wp, shift);
   } else {
     return cudaErrorInvalidValue;

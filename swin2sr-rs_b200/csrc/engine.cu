@@ -1,17 +1,17 @@
 // The forward pass behind the C ABI of include/s2s.h.
 //
 // Layout in HBM (per plan of B images, padded hp x wp, T = B*hp*wp tokens):
-//   residual stream X      fp32 [T][Cp] rows, in WINDOW-MAJOR order of the block's
-//                          shift (row b*hp*wp + wi*64 + t reads pixel Plan::index(wi,t,s)),
-//                          so the window partition/roll of src/cpu.rs:1148-1222 is a row
-//                          permutation applied by the epilogue that writes X;
-//   X16                    fp16 copy of X, the A operand of the next GEMM;
+//   residual stream X      fp32 [T][Cp] rows in image order (row b*hp*wp + y*wp + x),
+//                          updated in place by the epilogues of proj and fc2;
+//   X16                    fp16 copy of X, the A operand of the next GEMM / conv;
+//   window order           exists only inside the attention kernel, which gathers and
+//                          scatters token rows through the shift's row table (the
+//                          window partition and roll of src/cpu.rs:1148-1222);
 //   conv planes            NHWC fp16 [B][H][W][Cp], read by 4-D TMA boxes.
 // Cp = embed padded to 64 (pad lanes hold zeros), head_dim padded to DP = 16/32.
 //
 // Per block (src/cpu.rs:1516-1575): QKV GEMM -> window attention -> proj GEMM with
-// norm1 + residual -> fc1 GEMM + GELU -> fc2 GEMM with norm2 + residual, the last
-// one storing X in the NEXT block's window order (or image order at a stage end).
+// norm1 + residual -> fc1 GEMM + GELU -> fc2 GEMM with norm2 + residual.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -31,9 +31,9 @@
 
 namespace s2s {
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
-                                    const float* lscale, int nwin_total, int heads, int hd,
-                                    int dp, int ld_out, int nwh, int nww, int hp, int wp,
-                                    int shift, cudaStream_t st);
+                                    const float* lscale, const int* rows, int nwin_total,
+                                    int heads, int hd, int dp, int ld_out, int nwh, int nww,
+                                    int hp, int wp, int shift, cudaStream_t st);
 cudaError_t launch_pad_reflect(const float* x, float* y, int B, int c, int h, int w, int hp,
                                int wp, cudaStream_t st);
 cudaError_t launch_conv3_small(const float* in, const float* wgt, const float* bias, int B, int H,
@@ -92,17 +92,14 @@ struct Plan {
   size_t T = 0;
   std::vector<void*> allocs;
   size_t bytes = 0;
-  float *P = nullptr, *F0 = nullptr, *X[2] = {nullptr, nullptr}, *S = nullptr;
-  __half *F0h = nullptr, *X16[2] = {nullptr, nullptr}, *QKV = nullptr, *AO = nullptr,
-         *H16 = nullptr;
+  float *P = nullptr, *F0 = nullptr, *X = nullptr, *S = nullptr;
+  __half *F0h = nullptr, *X16 = nullptr, *QKV = nullptr, *AO = nullptr, *H16 = nullptr;
   __half *HA = nullptr, *HB[3] = {nullptr, nullptr, nullptr};
   float *BIC = nullptr, *BICF = nullptr, *AUXRAW = nullptr;
-  int* perm[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};  // see PERM_*
-  CUtensorMap mF0h, mX16[2], mAO, mH16, cX16[2], cAO, cHA;
+  int* rows[2] = {nullptr, nullptr};  // window-major token -> image row, shift 0 / win/2
+  CUtensorMap mF0h, mX16, mAO, mH16, cX16, cAO, cHA;
   CUtensorMap cHB[3][3];  // head planes at 1x, 2x, 4x resolution
 };
-
-enum { PERM_IMG_P0 = 0, PERM_P0_P4 = 1, PERM_P4_P0 = 2, PERM_P4_IMG = 3, PERM_P0_IMG = 4 };
 
 struct ProfEntry {
   const char* name;
@@ -393,10 +390,10 @@ int64_t plan_bytes(const s2s_handle* H, int B, int h, int w) {
   const int64_t Cp = H->Cp, s = H->cfg.scale;
   int64_t b = 0;
   b += (int64_t)B * 3 * hp * wp * 4;        // P
-  b += 4 * T * Cp * 4;                      // F0, X[2], S
-  b += 4 * T * Cp * 2;                      // F0h, X16[2], AO
+  b += 3 * T * Cp * 4;                      // F0, X, S
+  b += 3 * T * Cp * 2;                      // F0h, X16, AO
   b += T * H->NQ * 2 + T * H->HIDp * 2;     // QKV, H16
-  b += 5 * T * 4;                           // perms
+  b += 2 * T * 4;                           // window row tables
   b += T * 64 * 2 + 3 * T * s * s * 64 * 2; // head planes
   if (H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX)
     b += (int64_t)B * 3 * hp * s * wp * s * 4 + T * s * s * 64 * 4 + (int64_t)B * 3 * hp * wp * 4;
@@ -424,16 +421,14 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
   try {
     P->P = (float*)dalloc(*P, (size_t)B * 3 * hp * wp * 4);
     P->F0 = (float*)dalloc(*P, T * Cp * 4);
-    P->X[0] = (float*)dalloc(*P, T * Cp * 4);
-    P->X[1] = (float*)dalloc(*P, T * Cp * 4);
+    P->X = (float*)dalloc(*P, T * Cp * 4);
     P->S = (float*)dalloc(*P, T * Cp * 4);
     P->F0h = (__half*)dalloc(*P, T * Cp * 2);
-    P->X16[0] = (__half*)dalloc(*P, T * Cp * 2);
-    P->X16[1] = (__half*)dalloc(*P, T * Cp * 2);
+    P->X16 = (__half*)dalloc(*P, T * Cp * 2);
     P->AO = (__half*)dalloc(*P, T * Cp * 2);
     P->QKV = (__half*)dalloc(*P, T * H->NQ * 2);
     P->H16 = (__half*)dalloc(*P, T * H->HIDp * 2);
-    for (int i = 0; i < 5; i++) P->perm[i] = (int*)dalloc(*P, T * 4);
+    for (int i = 0; i < 2; i++) P->rows[i] = (int*)dalloc(*P, T * 4);
     P->HA = (__half*)dalloc(*P, T * 64 * 2);
     for (int i = 0; i < 3; i++) P->HB[i] = (__half*)dalloc(*P, T * s * s * 64 * 2);
     if (H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX) {
@@ -445,41 +440,29 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
     free_plan(*P);
     throw;
   }
-  // Row permutations (batch-offset): dst row of each source row.
+  // Window row tables (batch-offset): window-major token r of each image -> image row.
   {
     const int hw = hp * wp;
-    std::vector<int> m0(hw), m4(hw), inv0(hw), inv4(hw);
-    for (int r = 0; r < hw; r++) {
-      m0[r] = token_pixel(r, hp, wp, 0);
-      m4[r] = token_pixel(r, hp, wp, win / 2);
-    }
-    for (int r = 0; r < hw; r++) {
-      inv0[m0[r]] = r;
-      inv4[m4[r]] = r;
-    }
-    std::vector<int> pm[5];
-    for (auto& v : pm) v.resize(T);
+    std::vector<int> rt[2];
+    for (auto& v : rt) v.resize(T);
     for (int b = 0; b < B; b++) {
       const int o = b * hw;
       for (int r = 0; r < hw; r++) {
-        pm[PERM_IMG_P0][o + r] = o + inv0[r];
-        pm[PERM_P0_P4][o + r] = o + inv4[m0[r]];
-        pm[PERM_P4_P0][o + r] = o + inv0[m4[r]];
-        pm[PERM_P4_IMG][o + r] = o + m4[r];
-        pm[PERM_P0_IMG][o + r] = o + m0[r];
+        rt[0][o + r] = o + token_pixel(r, hp, wp, 0);
+        rt[1][o + r] = o + token_pixel(r, hp, wp, win / 2);
       }
     }
-    for (int i = 0; i < 5; i++)
-      ck(cudaMemcpy(P->perm[i], pm[i].data(), T * 4, cudaMemcpyHostToDevice), "perm upload");
+    for (int i = 0; i < 2; i++)
+      ck(cudaMemcpy(P->rows[i], rt[i].data(), T * 4, cudaMemcpyHostToDevice), "row table upload");
   }
   // TMA maps over the activation buffers.
   bool ok = true;
   ok &= make_map_rows(&P->mF0h, P->F0h, T, Cp, 128);
-  for (int i = 0; i < 2; i++) {
-    ok &= make_map_rows(&P->mX16[i], P->X16[i], T, Cp, 128);
+  {
+    ok &= make_map_rows(&P->mX16, P->X16, T, Cp, 128);
     int bw, bh;
     conv_box(wp, &bw, &bh);
-    ok &= make_map_nhwc(&P->cX16[i], P->X16[i], B, hp, wp, Cp, bw, bh);
+    ok &= make_map_nhwc(&P->cX16, P->X16, B, hp, wp, Cp, bw, bh);
   }
   ok &= make_map_rows(&P->mAO, P->AO, T, Cp, 128);
   ok &= make_map_rows(&P->mH16, P->H16, T, H->HIDp, 128);
@@ -611,18 +594,15 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.ln_b = H->pe_b;
     e.ln_n = C;
     e.n_valid = C;
-    e.o32 = P->X[0];
+    e.o32 = P->X;
     e.ld32 = Cp;
-    e.map32 = P->perm[PERM_IMG_P0];
-    e.o16 = P->X16[0];
+    e.o16 = P->X16;
     e.ld16 = Cp;
-    e.map16 = P->perm[PERM_IMG_P0];
     e.o32b = P->S;
     e.ld32b = Cp;
     GemmArgs a = gemm_args(M, Cp, Cp, e);
     L.run("gemm_patch_embed", [&] { return launch_gemm(P->mF0h, H->pe.map, a, Cp, st); });
   }
-  int cur = 0;
   const int nwin = B * (hp / 8) * (wp / 8);
   for (int si = 0; si < c.n_depths; si++) {
     Stage& stg = H->stages[si];
@@ -630,24 +610,17 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     for (int b = 0; b < depth; b++) {
       Block& bl = stg.blocks[b];
       const int sh = (b % 2 == 1) ? c.window / 2 : 0;
-      const int* out_map;
-      if (b + 1 < depth) {
-        const int sh2 = ((b + 1) % 2 == 1) ? c.window / 2 : 0;
-        out_map = sh == sh2 ? nullptr : (sh == 0 ? P->perm[PERM_P0_P4] : P->perm[PERM_P4_P0]);
-      } else {
-        out_map = sh == 0 ? P->perm[PERM_P0_IMG] : P->perm[PERM_P4_IMG];
-      }
       {  // QKV
         Epi e = epi0();
         e.bias = bl.qkv.b;
         e.o16 = P->QKV;
         e.ld16 = H->NQ;
         GemmArgs a = gemm_args(M, H->NQ, Cp, e);
-        L.run("gemm_qkv", [&] { return launch_gemm(P->mX16[cur], bl.qkv.map, a, bl.qkv.BN, st); });
+        L.run("gemm_qkv", [&] { return launch_gemm(P->mX16, bl.qkv.map, a, bl.qkv.BN, st); });
       }
       L.run("window_attention", [&] {
-        return launch_window_attention(P->QKV, P->AO, bl.cpb, bl.ls, nwin, H->heads, H->hd, H->DP,
-                                       Cp, hp / 8, wp / 8, hp, wp, sh, st);
+        return launch_window_attention(P->QKV, P->AO, bl.cpb, bl.ls, P->rows[sh ? 1 : 0], nwin,
+                                       H->heads, H->hd, H->DP, Cp, hp / 8, wp / 8, hp, wp, sh, st);
       });
       {  // proj + norm1 + residual, in place
         Epi e = epi0();
@@ -656,11 +629,11 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.ln_b = bl.n1b;
         e.ln_n = C;
         e.n_valid = C;
-        e.res_post = P->X[cur];
+        e.res_post = P->X;
         e.ld_res_post = Cp;
-        e.o32 = P->X[cur];
+        e.o32 = P->X;
         e.ld32 = Cp;
-        e.o16 = P->X16[cur];
+        e.o16 = P->X16;
         e.ld16 = Cp;
         GemmArgs a = gemm_args(M, Cp, Cp, e);
         L.run("gemm_proj", [&] { return launch_gemm(P->mAO, bl.proj.map, a, Cp, st); });
@@ -672,27 +645,24 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.o16 = P->H16;
         e.ld16 = H->HIDp;
         GemmArgs a = gemm_args(M, H->HIDp, Cp, e);
-        L.run("gemm_fc1", [&] { return launch_gemm(P->mX16[cur], bl.fc1.map, a, bl.fc1.BN, st); });
+        L.run("gemm_fc1", [&] { return launch_gemm(P->mX16, bl.fc1.map, a, bl.fc1.BN, st); });
       }
-      {  // fc2 + norm2 + residual -> next block's window order
+      {  // fc2 + norm2 + residual, in place
         Epi e = epi0();
         e.bias = bl.fc2.b;
         e.ln_g = bl.n2g;
         e.ln_b = bl.n2b;
         e.ln_n = C;
         e.n_valid = C;
-        e.res_post = P->X[cur];
+        e.res_post = P->X;
         e.ld_res_post = Cp;
-        e.o32 = P->X[1 - cur];
+        e.o32 = P->X;
         e.ld32 = Cp;
-        e.map32 = out_map;
-        e.o16 = P->X16[1 - cur];
+        e.o16 = P->X16;
         e.ld16 = Cp;
-        e.map16 = out_map;
         GemmArgs a = gemm_args(M, Cp, H->HIDp, e);
         L.run("gemm_fc2", [&] { return launch_gemm(P->mH16, bl.fc2.map, a, Cp, st); });
       }
-      cur = 1 - cur;
     }
     // RSTB tail: conv3x3 -> 1x1 patch_embed + stage residual.
     {
@@ -702,7 +672,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       e.o16 = P->AO;
       e.ld16 = Cp;
       GemmArgs a = conv_args(B, hp, wp, Cp, Cp, e);
-      L.run("conv_stage", [&] { return launch_gemm(P->cX16[cur], stg.conv.map, a, Cp, st); });
+      L.run("conv_stage", [&] { return launch_gemm(P->cX16, stg.conv.map, a, Cp, st); });
     }
     {
       const bool last = si + 1 == c.n_depths;
@@ -712,19 +682,17 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       e.res_pre = P->S;
       e.ld_res_pre = Cp;
       if (!last) {
-        e.o32 = P->X[cur];
+        e.o32 = P->X;
         e.ld32 = Cp;
-        e.map32 = P->perm[PERM_IMG_P0];
-        e.o16 = P->X16[cur];
+        e.o16 = P->X16;
         e.ld16 = Cp;
-        e.map16 = P->perm[PERM_IMG_P0];
         e.o32b = P->S;
         e.ld32b = Cp;
       } else {  // + final norm, image order, fp16 operand of conv_after_body
         e.ln_g = H->nrm_g;
         e.ln_b = H->nrm_b;
         e.ln_n = C;
-        e.o16 = P->X16[cur];
+        e.o16 = P->X16;
         e.ld16 = Cp;
       }
       GemmArgs a = gemm_args(M, Cp, Cp, e);
@@ -742,7 +710,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.o16 = P->AO;
     e.ld16 = Cp;
     GemmArgs a = conv_args(B, hp, wp, Cp, Cp, e);
-    L.run("conv_after_body", [&] { return launch_gemm(P->cX16[cur], H->cab.map, a, Cp, st); });
+    L.run("conv_after_body", [&] { return launch_gemm(P->cX16, H->cab.map, a, Cp, st); });
   }
   // 4. head.
   auto conv_to = [&](const char* name, const CUtensorMap& mapA, const TcWeight& tw, int Hh, int Ww,
@@ -1077,12 +1045,10 @@ int64_t s2s_debug_read(s2s_handle* H, const char* name, float* host, int64_t cap
   const std::string k(name);
   if (k == "P") { p = P.P; n = (size_t)P.B * 3 * P.hp * P.wp; }
   else if (k == "F0") { p = P.F0; n = T * Cp; }
-  else if (k == "X0") { p = P.X[0]; n = T * Cp; }
-  else if (k == "X1") { p = P.X[1]; n = T * Cp; }
+  else if (k == "X") { p = P.X; n = T * Cp; }
   else if (k == "S") { p = P.S; n = T * Cp; }
   else if (k == "F0h") { p = P.F0h; n = T * Cp; half = true; }
-  else if (k == "X16_0") { p = P.X16[0]; n = T * Cp; half = true; }
-  else if (k == "X16_1") { p = P.X16[1]; n = T * Cp; half = true; }
+  else if (k == "X16") { p = P.X16; n = T * Cp; half = true; }
   else if (k == "QKV") { p = P.QKV; n = T * H->NQ; half = true; }
   else if (k == "AO") { p = P.AO; n = T * Cp; half = true; }
   else if (k == "H16") { p = P.H16; n = T * H->HIDp; half = true; }
