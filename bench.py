@@ -73,6 +73,7 @@ def kernel_flops(wt, B, hp, wp):
         "gemm_proj": 2 * T * C * C,
         "gemm_fc1": 2 * T * C * m * C,
         "gemm_fc2": 2 * T * m * C * C,
+        "mlp_fused": 2 * 2 * T * C * m * C,
         "conv_stage": 2 * T * 9 * C * C,
         "gemm_stage_pe": 2 * T * C * C,
         "gemm_stage_pe_norm": 2 * T * C * C,

@@ -133,6 +133,7 @@ struct s2s_handle {
   std::vector<cudaEvent_t> ev_pool;
   std::map<std::string, std::pair<long, double>> prof;
   long long launches = 0;
+  bool fused_mlp = false;      // (Cp, HIDp) has a fused MLP kernel
   long long stop_after = -1;   // diagnostics: launches per forward before stopping
   long long fwd_launches = 0;  // launches enqueued by the forward in flight
 };
@@ -638,30 +639,46 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         GemmArgs a = gemm_args(M, Cp, Cp, e);
         L.run("gemm_proj", [&] { return launch_gemm(P->mAO, bl.proj.map, a, Cp, st); });
       }
-      {  // fc1 + GELU
-        Epi e = epi0();
-        e.bias = bl.fc1.b;
-        e.act = ACT_GELU;
-        e.o16 = P->H16;
-        e.ld16 = H->HIDp;
-        GemmArgs a = gemm_args(M, H->HIDp, Cp, e);
-        L.run("gemm_fc1", [&] { return launch_gemm(P->mX16, bl.fc1.map, a, bl.fc1.BN, st); });
-      }
-      {  // fc2 + norm2 + residual, in place
-        Epi e = epi0();
-        e.bias = bl.fc2.b;
-        e.ln_g = bl.n2g;
-        e.ln_b = bl.n2b;
-        e.ln_n = C;
-        e.n_valid = C;
-        e.res_post = P->X;
-        e.ld_res_post = Cp;
-        e.o32 = P->X;
-        e.ld32 = Cp;
-        e.o16 = P->X16;
-        e.ld16 = Cp;
-        GemmArgs a = gemm_args(M, Cp, H->HIDp, e);
-        L.run("gemm_fc2", [&] { return launch_gemm(P->mH16, bl.fc2.map, a, Cp, st); });
+      if (H->fused_mlp) {  // fc1 + GELU + fc2 + norm2 + residual in one kernel
+        MlpArgs m;
+        m.M = M;
+        m.b1 = bl.fc1.b;
+        m.b2 = bl.fc2.b;
+        m.g2 = bl.n2g;
+        m.beta2 = bl.n2b;
+        m.ln_n = C;
+        m.ln_eps = 1e-5f;
+        m.x = P->X;
+        m.x16 = P->X16;
+        L.run("mlp_fused", [&] {
+          return launch_mlp(P->mX16, bl.fc1.map, bl.fc2.map, m, Cp, H->HIDp, st);
+        });
+      } else {
+        {  // fc1 + GELU
+          Epi e = epi0();
+          e.bias = bl.fc1.b;
+          e.act = ACT_GELU;
+          e.o16 = P->H16;
+          e.ld16 = H->HIDp;
+          GemmArgs a = gemm_args(M, H->HIDp, Cp, e);
+          L.run("gemm_fc1", [&] { return launch_gemm(P->mX16, bl.fc1.map, a, bl.fc1.BN, st); });
+        }
+        {  // fc2 + norm2 + residual, in place
+          Epi e = epi0();
+          e.bias = bl.fc2.b;
+          e.ln_g = bl.n2g;
+          e.ln_b = bl.n2b;
+          e.ln_n = C;
+          e.n_valid = C;
+          e.res_post = P->X;
+          e.ld_res_post = Cp;
+          e.o32 = P->X;
+          e.ld32 = Cp;
+          e.o16 = P->X16;
+          e.ld16 = Cp;
+          GemmArgs a = gemm_args(M, Cp, H->HIDp, e);
+          L.run("gemm_fc2", [&] { return launch_gemm(P->mH16, bl.fc2.map, a, Cp, st); });
+        }
       }
     }
     // RSTB tail: conv3x3 -> 1x1 patch_embed + stage residual.
@@ -920,6 +937,11 @@ int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, 
   if (H->NQ % 32 != 0 || H->HIDp % 32 != 0) {
     g_create_error = "s2s_create: unsupported padded widths";
     return S2S_ERR_UNSUPPORTED;
+  }
+  H->fused_mlp = (H->Cp == 192 && H->HIDp == 384) || (H->Cp == 64 && H->HIDp == 128);
+  {
+    const char* f = getenv("S2S_UNFUSED_MLP");  // validation switch: the two-GEMM MLP path
+    if (f && *f && strcmp(f, "0") != 0) H->fused_mlp = false;
   }
   TensorTable T;
   for (int i = 0; i < n_tensors; i++) T.t[tensors[i].name] = &tensors[i];

@@ -70,6 +70,25 @@ struct GemmArgs {
 cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& a,
                         int BN, cudaStream_t st);
 
+// Fused MLP sublayer (csrc/mlp.cu): X <- X + LN(fc2(GELU(fc1(X16)))) in place.
+struct MlpArgs {
+  int M;                 // tokens
+  const float* b1;       // [HP] fc1 bias (padded)
+  const float* b2;       // [CP] fc2 bias
+  const float* g2;       // [CP] norm2 weight (zero in the pad)
+  const float* beta2;    // [CP] norm2 bias
+  int ln_n;              // real channels
+  float ln_eps;
+  float* x;              // [M][CP] fp32 residual stream, updated in place
+  __half* x16;           // [M][CP] fp16 copy, updated in place
+};
+
+// mapX: rows map of x16 (box 128 rows); mapW1: fc1 weight [HP][CP] (box N1 rows);
+// mapW2: fc2 weight [CP][HP] (box CP rows). Supported (cp, hp): (192, 384), (64, 128).
+cudaError_t launch_mlp(const CUtensorMap& mapX, const CUtensorMap& mapW1,
+                       const CUtensorMap& mapW2, const MlpArgs& a, int cp, int hp,
+                       cudaStream_t st);
+
 // TMA descriptor helpers (driver entry point resolved at first use).
 bool make_map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols_padded,
                    uint32_t box_rows);
