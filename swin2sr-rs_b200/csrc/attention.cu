@@ -1,9 +1,14 @@
 // SwinV2 scaled-cosine window attention (reference: src/cpu.rs:1244-1402,
 // tools/network_swin2sr.py:151-190).
 //
-// One CTA per 8x8 window, eight warps. The reciprocal L2 norms of every q and k
-// row of every head are computed once per window; then each warp takes (head,
-// 16-query-row block) tasks independently. Per task:
+// Persistent CTAs, each owning a group of HPC heads and walking windows: one producer
+// warp and 4*HPC compute warps, one (head, 16-query-row block) task per compute warp
+// and window, with no block-wide barrier in the window loop. The group's position-bias
+// table ([HPC][64][72] fp32, rows padded for conflict-free reads) is brought into
+// shared memory once; the producer gathers each window's q/k/v rows of those heads by
+// bulk copies into one of two buffers (full/empty mbarriers), so the next window's
+// copies overlap this window's math. Each compute warp derives the reciprocal L2 norms
+// it needs from the same fp16 values the MMAs read, then:
 //   S = Q K^T          mma.sync m16n8k16 fp16 -> fp32 (16 x 64 per warp, in registers)
 //   s = S * (1/|q|) * (1/|k|) * exp(min(logit_scale, ln 100)) + cpb[h][q][k]  (- 100 across shift
 //       regions; the region of a token is computed from its rolled plane coordinate)
@@ -13,7 +18,7 @@
 // The residual stream and every token-row buffer stay in image order; this kernel
 // is the only place the window partition and cyclic roll exist: `rows` maps the
 // window-major token (b, wi, t) of the block's shift to its image row
-// (src/plan.rs:72-78), so the window's q/k/v rows (fp16, [3][heads][DP] per token,
+// (src/plan.rs:72-78), so the window's q/k/v rows (fp16, [heads][q|k|v][DP] per token,
 // pad lanes zero) are gathered with one bulk copy per token row into a padded,
 // bank-conflict-free shared-memory layout, and outputs are scattered back to the
 // same rows.
@@ -63,66 +68,117 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
-// DP: padded head dim (16 or 32). Window of 64 tokens (win = 8).
-template <int DP>
-__global__ void __launch_bounds__(256) k_window_attention(
+// DP: padded head dim (16 or 32); HPC heads per CTA. Window of 64 tokens (win = 8).
+template <int DP, int HPC>
+__global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     const __half* __restrict__ qkv, __half* __restrict__ out, const float* __restrict__ cpb,
     const float* __restrict__ lscale, const int* __restrict__ rows, int heads, int hd, int ld_out,
-    int nwh, int nww, int hp, int wp, int shift) {
+    int nwh, int nww, int hp, int wp, int shift, int nwin_total) {
   constexpr int N = 64;
-  const int row_h = 3 * heads * DP;            // halves per token row
-  const int row_bytes = row_h * 2;
-  const int sstride = row_h + 8;               // padded smem row (halves): odd number of 16 B
+  constexpr int NS = N + 8;                    // padded bias row (floats)
+  constexpr int SEG = HPC * 3 * DP;            // halves of this CTA's heads per token row
+  constexpr int SSTRIDE = SEG + 8;             // padded smem row: odd number of 16 B units
+  constexpr int CW = 4 * HPC;                  // compute warps
   extern __shared__ uint8_t smem_raw[];
-  __half* sq = reinterpret_cast<__half*>(smem_raw);
-  // [heads][2][64]: 1/|k| then 1/|q| per head
-  float* snorm = reinterpret_cast<float*>(smem_raw + (size_t)N * sstride * 2);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(snorm + 2 * N * heads);
+  float* scpb = reinterpret_cast<float*>(smem_raw);                       // [HPC][64][NS]
+  __half* sqb = reinterpret_cast<__half*>(scpb + HPC * N * NS);           // [2][64][SSTRIDE]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sqb + 2 * N * SSTRIDE);    // [2]
+  uint64_t* empty = full + 2;                                             // [2]
+  uint64_t* cbar = empty + 2;                                             // bias table
 
-  const int win_idx = blockIdx.x;              // global window (image-major)
+  const int NG = heads / HPC;
+  const int h0 = (blockIdx.x % NG) * HPC;     // first head of this CTA
+  const int wstep = gridDim.x / NG;           // host launches a multiple of NG CTAs
   const int nw = nwh * nww;
-  const int wi = win_idx % nw;
-  const int wh = wi / nww, ww = wi % nww;
-  const size_t tok0 = (size_t)win_idx * N;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, t4 = lane & 3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row_h = 3 * heads * DP;            // halves per full QKV token row
+  const int win0 = blockIdx.x / NG;
 
-  if (tid == 0) {
-    mbar_init(bar, 1);
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&full[b], 1);
+      mbar_init(&empty[b], CW);
+    }
+    mbar_init(cbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
-  if (tid == 0) mbar_arrive_expect_tx(bar, (uint32_t)(N * row_bytes));
-  __syncthreads();
-  if (tid < N)
-    bulk_g2s(sq + (size_t)tid * sstride, qkv + (size_t)rows[tok0 + tid] * row_h, row_bytes, bar);
-  const bool ok = mbar_wait(bar, 0, DEV_TIMEOUT_FULL);
-  if (!__syncthreads_and(ok)) return;  // uniform exit: no thread is left at a barrier
 
-  // Reciprocal norms of every head's q and k rows, from the same fp16 values the MMAs read.
-  for (int idx = tid; idx < 2 * N * heads; idx += blockDim.x) {
-    const int h = idx / (2 * N), rem = idx - h * 2 * N;
-    const int isq = rem >= N, tok = rem & (N - 1);
-    const __half* v = sq + (size_t)tok * sstride + (isq ? h : heads + h) * DP;
-    float acc = 0.0f;
-    for (int d = 0; d < hd; d++) {
-      const float x = __half2float(v[d]);
-      acc += x * x;
+  if (warp == CW) {
+    // ------------------------------------------------------------ producer warp
+    if (lane == 0) {
+      mbar_arrive_expect_tx(cbar, (uint32_t)(HPC * N * NS * 4));
+      bulk_g2s(scpb, cpb + (size_t)h0 * N * NS, HPC * N * NS * 4, cbar);
     }
-    snorm[idx] = 1.0f / fmaxf(sqrtf(acc), 1e-12f);
+    int i = 0;
+    for (int win = win0; win < nwin_total; win += wstep, i++) {
+      const int b = i & 1;
+      // rows of this window (loaded before waiting, so their latency overlaps the wait)
+      const int r0 = rows[(size_t)win * N + lane], r1 = rows[(size_t)win * N + 32 + lane];
+      if (i >= 2 && !mbar_wait(&empty[b], ((i >> 1) - 1) & 1, DEV_TIMEOUT_EMPTY)) break;
+      if (lane == 0) mbar_arrive_expect_tx(&full[b], (uint32_t)(N * SEG * 2));
+      __syncwarp();
+      __half* dst = sqb + (size_t)b * N * SSTRIDE;
+      bulk_g2s(dst + (size_t)lane * SSTRIDE, qkv + (size_t)r0 * row_h + h0 * 3 * DP, SEG * 2, &full[b]);
+      bulk_g2s(dst + (size_t)(32 + lane) * SSTRIDE, qkv + (size_t)r1 * row_h + h0 * 3 * DP, SEG * 2,
+               &full[b]);
+    }
+    return;
   }
-  __syncthreads();
 
-  const uint32_t sbase = smem_u32(sq);
-  for (int task = warp; task < heads * 4; task += 8) {
-    const int h = task >> 2, rb = task & 3;
-    const int qr0 = rb * 16 + g, qr1 = qr0 + 8;
+  // -------------------------------------------------------------- compute warps
+  const int g = lane >> 2, t4 = lane & 3;
+  const int hl = warp >> 2, rb = warp & 3;     // this warp's task in every window
+  const int h = h0 + hl;
+  const int qr0 = rb * 16 + g, qr1 = qr0 + 8;
+  const int qoff = hl * 3 * DP, koff = qoff + DP, voff = qoff + 2 * DP;
+  const float ls = lscale[h];
+  const float* cp0 = scpb + ((size_t)hl * N + qr0) * NS;
+  const float* cp1 = scpb + ((size_t)hl * N + qr1) * NS;
+  const uint32_t sbase0 = smem_u32(sqb);
+  bool ok = mbar_wait(cbar, 0, DEV_TIMEOUT_FULL);
+  auto inv_norm = [&](const __half* p) {
+    const uint4* v = reinterpret_cast<const uint4*>(p);
+    float acc[DP / 8];
+#pragma unroll
+    for (int k = 0; k < DP / 8; k++) {
+      const uint4 u = v[k];
+      const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+      float a = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float2 f = __half22float2(h2[e]);
+        a += f.x * f.x;
+        a += f.y * f.y;
+      }
+      acc[k] = a;
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < DP / 8; k++) sum += acc[k];
+    return 1.0f / fmaxf(sqrtf(sum), 1e-12f);
+  };
+
+  int i = 0;
+  for (int win = win0; win < nwin_total && ok; win += wstep, i++) {
+    const int b = i & 1;
+    if (!mbar_wait(&full[b], (i >> 1) & 1, DEV_TIMEOUT_FULL)) break;
+    const __half* sq = sqb + (size_t)b * N * SSTRIDE;
+    const uint32_t sbase = sbase0 + (uint32_t)(b * N * SSTRIDE * 2);
+    const int wi = win % nw;
+    const int wh = wi / nww, ww = wi % nww;
+    const size_t tok0 = (size_t)win * N;
+
+    // 1/|k| for keys lane and lane+32, 1/|q| for this thread's two query rows.
+    const float kn_lo = inv_norm(sq + (size_t)lane * SSTRIDE + koff);
+    const float kn_hi = inv_norm(sq + (size_t)(32 + lane) * SSTRIDE + koff);
+    const float qs0 = inv_norm(sq + (size_t)qr0 * SSTRIDE + qoff) * ls;
+    const float qs1 = inv_norm(sq + (size_t)qr1 * SSTRIDE + qoff) * ls;
     int qreg0 = 0, qreg1 = 0;
     if (shift) {
       qreg0 = 3 * region_of(wh * 8 + qr0 / 8, hp, 8, shift) + region_of(ww * 8 + qr0 % 8, wp, 8, shift);
       qreg1 = 3 * region_of(wh * 8 + qr1 / 8, hp, 8, shift) + region_of(ww * 8 + qr1 % 8, wp, 8, shift);
     }
-    const int qoff = h * DP, koff = (heads + h) * DP, voff = (2 * heads + h) * DP;
 
     // S = Q K^T for 16 rows x 64 keys.
     float sacc[8][4];
@@ -133,31 +189,28 @@ __global__ void __launch_bounds__(256) k_window_attention(
       uint32_t a0, a1, a2, a3;
       const int arow = rb * 16 + (lane & 15);
       const int acol = qoff + kk * 16 + (lane >> 4) * 8;
-      ldsm_x4(sbase + (uint32_t)((arow * sstride + acol) * 2), a0, a1, a2, a3);
+      ldsm_x4(sbase + (uint32_t)((arow * SSTRIDE + acol) * 2), a0, a1, a2, a3);
 #pragma unroll
       for (int j = 0; j < 8; j += 2) {
         uint32_t b0, b1, b2, b3;
         const int krow = 8 * j + (lane & 7) + ((lane >> 4) << 3);
         const int kcol = koff + kk * 16 + ((lane >> 3) & 1) * 8;
-        ldsm_x4(sbase + (uint32_t)((krow * sstride + kcol) * 2), b0, b1, b2, b3);
+        ldsm_x4(sbase + (uint32_t)((krow * SSTRIDE + kcol) * 2), b0, b1, b2, b3);
         mma16816(sacc[j], a0, a1, a2, a3, b0, b1);
         mma16816(sacc[j + 1], a0, a1, a2, a3, b2, b3);
       }
     }
 
     // Scale, bias, mask, softmax.
-    const float ls = lscale[h];
-    const float* kinv = snorm + h * 2 * N;
-    const float qs0 = kinv[N + qr0] * ls, qs1 = kinv[N + qr1] * ls;
-    const float* cp0 = cpb + ((size_t)h * N + qr0) * N;
-    const float* cp1 = cpb + ((size_t)h * N + qr1) * N;
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       const int k = 8 * j + 2 * t4;
-      const float ki0 = kinv[k], ki1 = kinv[k + 1];
-      const float2 b0 = __ldg(reinterpret_cast<const float2*>(cp0 + k));
-      const float2 b1 = __ldg(reinterpret_cast<const float2*>(cp1 + k));
+      // key k lives in lane k % 32 (low half for j < 4, high half otherwise)
+      const float ki0 = __shfl_sync(0xffffffffu, j < 4 ? kn_lo : kn_hi, k & 31);
+      const float ki1 = __shfl_sync(0xffffffffu, j < 4 ? kn_lo : kn_hi, (k + 1) & 31);
+      const float2 b0 = *reinterpret_cast<const float2*>(cp0 + k);
+      const float2 b1 = *reinterpret_cast<const float2*>(cp1 + k);
       float s00 = sacc[j][0] * ki0 * qs0 + b0.x;
       float s01 = sacc[j][1] * ki1 * qs0 + b0.y;
       float s10 = sacc[j][2] * ki0 * qs1 + b1.x;
@@ -212,11 +265,14 @@ __global__ void __launch_bounds__(256) k_window_attention(
         uint32_t b0, b1, b2, b3;
         const int vrow = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
         const int vcol = voff + n * 8 + ((lane >> 4) << 3);
-        ldsm_x4_t(sbase + (uint32_t)((vrow * sstride + vcol) * 2), b0, b1, b2, b3);
+        ldsm_x4_t(sbase + (uint32_t)((vrow * SSTRIDE + vcol) * 2), b0, b1, b2, b3);
         mma16816(oacc[n], a0, a1, a2, a3, b0, b1);
         mma16816(oacc[n + 1], a0, a1, a2, a3, b2, b3);
       }
     }
+    // this warp is done with the buffer
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[b]);
     const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
     __half* o0 = out + (size_t)rows[tok0 + qr0] * ld_out + h * hd;
     __half* o1 = out + (size_t)rows[tok0 + qr1] * ld_out + h * hd;
@@ -233,36 +289,56 @@ __global__ void __launch_bounds__(256) k_window_attention(
   }
 }
 
+template <int DP, int HPC>
+cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb, const float* lscale,
+                          const int* rows, int nwin_total, int heads, int hd, int ld_out, int nwh,
+                          int nww, int hp, int wp, int shift, cudaStream_t st) {
+  constexpr int SEG = HPC * 3 * DP;
+  const size_t smem = (size_t)HPC * 64 * 72 * 4 + (size_t)2 * 64 * (SEG + 8) * 2 + 5 * 8 + 16;
+  static int ctas = 0;  // resident CTAs per device
+  if (ctas == 0) {
+    cudaError_t err = cudaFuncSetAttribute(k_window_attention<DP, HPC>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    int dev = 0, sms = 0, occ = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_window_attention<DP, HPC>,
+                                                        128 * HPC + 32, smem);
+    if (err != cudaSuccess) return err;
+    if (occ < 1) return cudaErrorInvalidConfiguration;
+    ctas = sms * occ;
+  }
+  const int NG = heads / HPC;
+  long G = (long)nwin_total * NG;
+  if (G > ctas) G = ctas;
+  G = (G / NG) * NG;
+  if (G < NG) G = NG;
+  k_window_attention<DP, HPC><<<(unsigned)G, 128 * HPC + 32, smem, st>>>(
+      qkv, out, cpb, lscale, rows, heads, hd, ld_out, nwh, nww, hp, wp, shift, nwin_total);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
                                     const float* lscale, const int* rows, int nwin_total,
                                     int heads, int hd, int dp, int ld_out, int nwh, int nww,
                                     int hp, int wp, int shift, cudaStream_t st) {
-  const int row_h = 3 * heads * dp;
-  const size_t smem = (size_t)64 * (row_h + 8) * 2 + 2 * 64 * heads * 4 + 16;
-  if (dp == 32) {
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(k_window_attention<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-      set = true;
-    }
-    k_window_attention<32><<<nwin_total, 256, smem, st>>>(qkv, out, cpb, lscale, rows, heads, hd,
-                                                          ld_out, nwh, nww, hp, wp, shift);
-  } else if (dp == 16) {
-    static bool set = false;
-    if (!set) {
-      cudaFuncSetAttribute(k_window_attention<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-      set = true;
-    }
-    k_window_attention<16><<<nwin_total, 256, smem, st>>>(qkv, out, cpb, lscale, rows, heads, hd,
-                                                          ld_out, nwh, nww, hp, wp, shift);
-  } else {
-    return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  const bool pair = heads % 2 == 0;
+  if (dp == 32 && pair)
+    return launch_attn_t<32, 2>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
+                                nww, hp, wp, shift, st);
+  if (dp == 32)
+    return launch_attn_t<32, 1>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
+                                nww, hp, wp, shift, st);
+  if (dp == 16 && pair)
+    return launch_attn_t<16, 2>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
+                                nww, hp, wp, shift, st);
+  if (dp == 16)
+    return launch_attn_t<16, 1>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
+                                nww, hp, wp, shift, st);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace s2s

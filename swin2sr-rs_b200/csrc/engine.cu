@@ -256,7 +256,8 @@ void build_weights(s2s_handle* H, const TensorTable& T) {
       char pfx[96];
       snprintf(pfx, sizeof pfx, "layers.%d.residual_group.blocks.%d.", s, b);
       const std::string p(pfx);
-      // QKV: rows [3][heads][DP] <- [3C] (q, k, v), pad lanes zero.
+      // QKV: rows [heads][q|k|v][DP] <- [3C] (q, k, v), pad lanes zero, so one head's
+      // q, k and v of a token are one contiguous run for the attention kernel.
       const float* wq = T.get(p + "attn.qkv.wq", (int64_t)C * C);
       const float* wk = T.get(p + "attn.qkv.wk", (int64_t)C * C);
       const float* wv = T.get(p + "attn.qkv.wv", (int64_t)C * C);
@@ -273,7 +274,7 @@ void build_weights(s2s_handle* H, const TensorTable& T) {
       std::vector<int> qmap(H->NQ, -1);
       for (int part = 0; part < 3; part++)
         for (int h = 0; h < heads; h++)
-          for (int d = 0; d < hd; d++) qmap[(part * heads + h) * DP + d] = part * C + h * hd + d;
+          for (int d = 0; d < hd; d++) qmap[(h * 3 + part) * DP + d] = part * C + h * hd + d;
       pack_linear(H, bl.qkv, W3.data(), b3.data(), C, H->NQ, Cp, n_tile_for(H->NQ), qmap);
       pack_linear(H, bl.proj, T.get(p + "attn.proj.weight", (int64_t)C * C),
                   T.get(p + "attn.proj.bias", C), C, Cp, Cp, Cp, identity_rows(Cp, C));
@@ -286,13 +287,16 @@ void build_weights(s2s_handle* H, const TensorTable& T) {
       bl.n1b = upload(H, padded(T.get(p + "norm1.bias", C), C, Cp));
       bl.n2g = upload(H, padded(T.get(p + "norm2.weight", C), C, Cp));
       bl.n2b = upload(H, padded(T.get(p + "norm2.bias", C), C, Cp));
-      // cpb_pre [N*N][heads] -> [heads][N][N]; logit scale -> exp(min(ls, ln 100)).
+      // cpb_pre [N*N][heads] -> [heads][N][N + 8] (rows padded so that the attention
+      // kernel's shared-memory reads are free of bank conflicts); logit scale ->
+      // exp(min(ls, ln 100)).
       const float* cpb = T.get(p + "attn.cpb_pre", (int64_t)n * n * heads);
-      std::vector<float> cpbt((size_t)heads * n * n);
+      const int ns = n + 8;
+      std::vector<float> cpbt((size_t)heads * n * ns, 0.0f);
       for (int q = 0; q < n; q++)
         for (int k = 0; k < n; k++)
           for (int h = 0; h < heads; h++)
-            cpbt[((size_t)h * n + q) * n + k] = cpb[((size_t)q * n + k) * heads + h];
+            cpbt[((size_t)h * n + q) * ns + k] = cpb[((size_t)q * n + k) * heads + h];
       bl.cpb = upload(H, cpbt);
       const float* ls = T.get(p + "attn.logit_scale", heads);
       std::vector<float> lse(heads);
