@@ -20,6 +20,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <array>
 #include <map>
 #include <memory>
 #include <string>
@@ -99,6 +100,8 @@ struct Plan {
   int* rows[2] = {nullptr, nullptr};  // window-major token -> image row, shift 0 / win/2
   CUtensorMap mF0h, mX16, mAO, mH16, cX16, cAO, cHA;
   CUtensorMap cHB[3][3];  // head planes at 1x, 2x, 4x resolution
+  // Output / residual TMA maps, built on first use for each (buffer, geometry).
+  std::map<std::array<int64_t, 8>, CUtensorMap> omaps;
 };
 
 struct ProfEntry {
@@ -565,6 +568,32 @@ GemmArgs conv_args(int B, int H, int W, int Cip, int N, const Epi& e) {
   return a;
 }
 
+// The STORE_ROWS outputs and the post-norm residual of a launch, as TMA maps.
+OutMaps out_maps(Plan* P, const GemmArgs& a) {
+  OutMaps om;
+  memset(&om, 0, sizeof om);
+  if (a.epi.store != STORE_ROWS) return om;
+  auto mk = [&](CUtensorMap* m, const void* p, int eb, int ld) {
+    if (!p) return;
+    const std::array<int64_t, 8> key = {(int64_t)(uintptr_t)p, eb, ld, a.conv, a.conv ? a.B : a.M,
+                                        a.H, a.W, a.boxw};
+    auto it = P->omaps.find(key);
+    if (it == P->omaps.end()) {
+      CUtensorMap map;
+      const bool ok = a.conv ? make_map_out_nhwc(&map, p, eb, a.B, a.H, a.W, ld, a.boxw)
+                             : make_map_out_rows(&map, p, eb, (uint64_t)a.M, (uint64_t)ld);
+      if (!ok) fail(S2S_ERR_CUDA, "cuTensorMapEncodeTiled failed for an output operand");
+      it = P->omaps.emplace(key, map).first;
+    }
+    *m = it->second;
+  };
+  mk(&om.o32, a.epi.o32, 4, a.epi.ld32);
+  mk(&om.o32b, a.epi.o32b, 4, a.epi.ld32b);
+  mk(&om.o16, a.epi.o16, 2, a.epi.ld16);
+  if (a.epi.res_post) mk(&om.res, a.epi.res_post, 4, a.epi.ld_res_post);
+  return om;
+}
+
 void set_final(const s2s_handle* H, Epi& e) {
   e.img_range = H->cfg.img_range;
   e.mean0 = H->cfg.mean[0];
@@ -606,7 +635,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.o32b = P->S;
     e.ld32b = Cp;
     GemmArgs a = gemm_args(M, Cp, Cp, e);
-    L.run("gemm_patch_embed", [&] { return launch_gemm(P->mF0h, H->pe.map, a, Cp, st); });
+    L.run("gemm_patch_embed", [&] { return launch_gemm(P->mF0h, H->pe.map, out_maps(P, a), a, Cp, st); });
   }
   const int nwin = B * (hp / 8) * (wp / 8);
   for (int si = 0; si < c.n_depths; si++) {
@@ -621,7 +650,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.o16 = P->QKV;
         e.ld16 = H->NQ;
         GemmArgs a = gemm_args(M, H->NQ, Cp, e);
-        L.run("gemm_qkv", [&] { return launch_gemm(P->mX16, bl.qkv.map, a, bl.qkv.BN, st); });
+        L.run("gemm_qkv", [&] { return launch_gemm(P->mX16, bl.qkv.map, out_maps(P, a), a, bl.qkv.BN, st); });
       }
       L.run("window_attention", [&] {
         return launch_window_attention(P->QKV, P->AO, bl.cpb, bl.ls, P->rows[sh ? 1 : 0], nwin,
@@ -641,7 +670,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.o16 = P->X16;
         e.ld16 = Cp;
         GemmArgs a = gemm_args(M, Cp, Cp, e);
-        L.run("gemm_proj", [&] { return launch_gemm(P->mAO, bl.proj.map, a, Cp, st); });
+        L.run("gemm_proj", [&] { return launch_gemm(P->mAO, bl.proj.map, out_maps(P, a), a, Cp, st); });
       }
       if (H->fused_mlp) {  // fc1 + GELU + fc2 + norm2 + residual in one kernel
         MlpArgs m;
@@ -665,7 +694,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
           e.o16 = P->H16;
           e.ld16 = H->HIDp;
           GemmArgs a = gemm_args(M, H->HIDp, Cp, e);
-          L.run("gemm_fc1", [&] { return launch_gemm(P->mX16, bl.fc1.map, a, bl.fc1.BN, st); });
+          L.run("gemm_fc1", [&] { return launch_gemm(P->mX16, bl.fc1.map, out_maps(P, a), a, bl.fc1.BN, st); });
         }
         {  // fc2 + norm2 + residual, in place
           Epi e = epi0();
@@ -681,7 +710,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
           e.o16 = P->X16;
           e.ld16 = Cp;
           GemmArgs a = gemm_args(M, Cp, H->HIDp, e);
-          L.run("gemm_fc2", [&] { return launch_gemm(P->mH16, bl.fc2.map, a, Cp, st); });
+          L.run("gemm_fc2", [&] { return launch_gemm(P->mH16, bl.fc2.map, out_maps(P, a), a, Cp, st); });
         }
       }
     }
@@ -693,7 +722,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       e.o16 = P->AO;
       e.ld16 = Cp;
       GemmArgs a = conv_args(B, hp, wp, Cp, Cp, e);
-      L.run("conv_stage", [&] { return launch_gemm(P->cX16, stg.conv.map, a, Cp, st); });
+      L.run("conv_stage", [&] { return launch_gemm(P->cX16, stg.conv.map, out_maps(P, a), a, Cp, st); });
     }
     {
       const bool last = si + 1 == c.n_depths;
@@ -718,7 +747,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       }
       GemmArgs a = gemm_args(M, Cp, Cp, e);
       L.run(last ? "gemm_stage_pe_norm" : "gemm_stage_pe",
-            [&] { return launch_gemm(P->mAO, stg.pe.map, a, Cp, st); });
+            [&] { return launch_gemm(P->mAO, stg.pe.map, out_maps(P, a), a, Cp, st); });
     }
   }
   // 3. conv_after_body + body skip (conv_first output) -> Y16 (in AO).
@@ -731,13 +760,13 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.o16 = P->AO;
     e.ld16 = Cp;
     GemmArgs a = conv_args(B, hp, wp, Cp, Cp, e);
-    L.run("conv_after_body", [&] { return launch_gemm(P->cX16, H->cab.map, a, Cp, st); });
+    L.run("conv_after_body", [&] { return launch_gemm(P->cX16, H->cab.map, out_maps(P, a), a, Cp, st); });
   }
   // 4. head.
   auto conv_to = [&](const char* name, const CUtensorMap& mapA, const TcWeight& tw, int Hh, int Ww,
                      int Cip, Epi e) {
     GemmArgs a = conv_args(B, Hh, Ww, Cip, tw.N, e);
-    L.run(name, [&] { return launch_gemm(mapA, tw.map, a, tw.BN, st); });
+    L.run(name, [&] { return launch_gemm(mapA, tw.map, out_maps(P, a), a, tw.BN, st); });
   };
   auto cbu = [&]() {
     Epi e = epi0();

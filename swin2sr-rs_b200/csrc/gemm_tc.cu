@@ -27,7 +27,10 @@ namespace {
 
 constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
 constexpr int kEpiWarps = 8;
-constexpr int kStageFloats = 32 * 36;  // per epilogue warp: 32 rows x 32 cols, 16-B rows
+constexpr int kStageFloats = 32 * 36;  // STORE_SHUFFLE2 staging: 32 rows x 32 cols, 16-B rows
+// Per epilogue warp: two fp32 32x32 tiles (residual in, result out; 128-byte swizzle)
+// and two fp16 32x32 tiles (64-byte swizzle), double-buffered across chunks.
+constexpr int kWarpBuf = 2 * 4096 + 2 * 2048;
 
 template <int BN>
 struct TmemCols {
@@ -37,7 +40,7 @@ struct TmemCols {
 template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-           const GemmArgs a) {
+           const __grid_constant__ OutMaps om, const GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -45,15 +48,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int B_BYTES = BN * 128;
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  float* stage = reinterpret_cast<float*>(sB + STAGES * B_BYTES);
-  float* s_vec = stage + kEpiWarps * kStageFloats;          // bias, LN gamma, LN beta [3][BN]
-  int* s_rows = reinterpret_cast<int*>(s_vec + 3 * BN);     // per warp, per row: src, dst32, dst16, dst32b
+  uint8_t* obuf = sB + STAGES * B_BYTES;                    // [kEpiWarps][kWarpBuf], 1 KB aligned
+  float* s_vec = reinterpret_cast<float*>(obuf + kEpiWarps * kWarpBuf);  // bias, gamma, beta [3][BN]
+  int* s_rows = reinterpret_cast<int*>(s_vec + 3 * BN);     // shuffle store: per warp, per row
   uint64_t* full = reinterpret_cast<uint64_t*>(s_rows + kEpiWarps * 32 * 4);
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;   // [2] accumulator ready
   uint64_t* acce = accf + 2;         // [2] accumulator drained
   uint64_t* fin = acce + 2;          // all MMAs of this CTA retired
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(fin + 1);
+  uint64_t* rbar = fin + 1;          // [kEpiWarps][2] residual tile landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rbar + 2 * kEpiWarps);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -94,6 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acce[b], kEpiWarps);
     }
     mbar_init(fin, 1);
+    for (int k = 0; k < 2 * kEpiWarps; k++) mbar_init(&rbar[k], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -183,7 +188,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       s_vec[2 * BN + c] = (e.ln_n > 0 && col < e.ln_n) ? e.ln_b[col] : 0.0f;
     }
     asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
-    float* stg = stage + (warp - 2) * kStageFloats;
+    uint8_t* wbuf = obuf + (warp - 2) * kWarpBuf;
+    float* stg = reinterpret_cast<float*>(wbuf);  // STORE_SHUFFLE2 staging
+    uint64_t* wrb = rbar + 2 * (warp - 2);        // this warp's residual barriers
+    uint32_t jcnt = 0;                            // chunks this warp has processed (buffer parity)
+    if (STORE == STORE_ROWS && lane == 0) {
+      tma_prefetch_desc(&om.o32);
+      tma_prefetch_desc(&om.o16);
+    }
     int i = 0;
     for (int t = blockIdx.x; t < num_tiles; t += G, i++) {
     const int b = i & 1;
@@ -200,21 +212,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       valid = (py < a.H) && (px < a.W);
       mlog = (bimg * a.H + py) * a.W + px;
     }
-    {
+    if constexpr (STORE == STORE_SHUFFLE2) {
       int* rw = s_row + r * 4;
-      if constexpr (STORE == STORE_SHUFFLE2) {
-        rw[0] = valid ? mlog : -1;
-        rw[1] = (bimg * 2 * a.H + 2 * py) * (2 * a.W) + 2 * px;  // (dy, dx) = (0, 0) pixel
-        rw[2] = 0;
-        rw[3] = 0;
-      } else {
-        rw[0] = valid ? mlog : -1;
-        rw[1] = valid ? (e.map32 ? e.map32[mlog] : mlog) : 0;
-        rw[2] = valid ? (e.map16 ? e.map16[mlog] : mlog) : 0;
-        rw[3] = valid ? (e.map32b ? e.map32b[mlog] : mlog) : 0;
+      rw[0] = valid ? mlog : -1;
+      rw[1] = (bimg * 2 * a.H + 2 * py) * (2 * a.W) + 2 * px;  // (dy, dx) = (0, 0) pixel
+      __syncwarp();
+    }
+    // This warp's 32 rows as a TMA box origin: row m0 + 32q, or the conv sub-box.
+    const int orow = q * 32;
+    const int opx = a.conv ? x0 + (orow % a.boxw) : 0;
+    const int opy = a.conv ? y0 + orow / a.boxw : 0;
+    auto box_load_res = [&](void* dst, int col, uint64_t* bar) {
+      if (a.conv)
+        tma_load_4d(dst, &om.res, bar, col, opx, opy, bimg);
+      else
+        tma_load_2d(dst, &om.res, bar, col, m0 + orow);
+    };
+    auto box_store = [&](const CUtensorMap* m, const void* src, int col) {
+      if (a.conv)
+        tma_store_4d(m, src, col, opx, opy, bimg);
+      else
+        tma_store_2d(m, src, col, m0 + orow);
+    };
+    // Post-norm residual: the first chunk's tile is requested before the accumulator
+    // is ready, so its latency hides behind the MMAs.
+    if constexpr (STORE == STORE_ROWS && RES == 2) {
+      if (lane == 0 && half < BN / 32) {
+        bulk_wait_read<0>();
+        const int jb = jcnt & 1;
+        mbar_arrive_expect_tx(&wrb[jb], 4096);
+        box_load_res(wbuf + jb * 4096, n0 + half * 32, &wrb[jb]);
       }
     }
-    __syncwarp();
 
     const uint32_t tbase = tmem + (uint32_t)(b * BN) + ((uint32_t)(q * 32) << 16);
     const bool acc_ok = mbar_wait(&accf[b], (i >> 1) & 1, DEV_TIMEOUT_ACC);
@@ -234,7 +263,104 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* rpre = nullptr;
     if constexpr (RES == 1) rpre = e.res_pre + (size_t)(valid ? mlog : 0) * e.ld_res_pre + n0;
 
-    if constexpr (STORE == STORE_ROWS || STORE == STORE_SHUFFLE2) {
+    if constexpr (STORE == STORE_ROWS) {
+      float mean = 0.0f, rstd = 1.0f;
+      if constexpr (LN) {
+        float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; c++) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+#pragma unroll
+          for (int j = 0; j < 32; j++) {
+            float x = pre(v[j], c * 32 + j);
+            if constexpr (RES == 1) x += rpre[c * 32 + j];
+            s1 += x;
+            s2 += x * x;
+          }
+        }
+        const float nf = (float)e.ln_n;
+        mean = s1 / nf;
+        const float var = fmaxf(s2 / nf - mean * mean, 0.0f);
+        rstd = 1.0f / sqrtf(var + e.ln_eps);
+      }
+      const float nmr = -mean * rstd;
+      const int sw128 = lane & 7, sw64 = (lane >> 1) & 3;  // this row's swizzle phases
+#pragma unroll 1
+      for (int c = half; c < BN / 32; c += 2, jcnt++) {
+        const int jb = jcnt & 1;
+        float* f32 = reinterpret_cast<float*>(wbuf + jb * 4096);
+        uint8_t* f16 = wbuf + 8192 + jb * 2048;
+        float v[32];
+        tmem_ld32(tbase + c * 32, v);
+        if constexpr (RES == 2) {
+          // request the next chunk's residual into the other buffer, then wait for ours
+          if (lane == 0 && c + 2 < BN / 32) {
+            bulk_wait_read<0>();
+            mbar_arrive_expect_tx(&wrb[jb ^ 1], 4096);
+            box_load_res(wbuf + (jb ^ 1) * 4096, n0 + (c + 2) * 32, &wrb[jb ^ 1]);
+          }
+          if (!mbar_wait(&wrb[jb], (jcnt >> 1) & 1, DEV_TIMEOUT_FULL)) break;
+        } else {
+          if (lane == 0) bulk_wait_read<1>();  // this buffer's store two chunks ago
+          __syncwarp();
+        }
+        const int cl0 = c * 32;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          const float4 bb = *reinterpret_cast<const float4*>(s_vec + cl0 + 4 * u);
+          float x[4] = {v[4 * u] + bb.x, v[4 * u + 1] + bb.y, v[4 * u + 2] + bb.z,
+                        v[4 * u + 3] + bb.w};
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            if constexpr (ACT == ACT_GELU) x[k] = 0.5f * x[k] * (1.0f + erff(x[k] * 0.70710678118654752440f));
+            if constexpr (ACT == ACT_LRELU) x[k] = x[k] < 0.0f ? x[k] * e.slope : x[k];
+            if constexpr (RES == 1) x[k] += rpre[cl0 + 4 * u + k];
+          }
+          if constexpr (LN) {
+            const float4 gg = *reinterpret_cast<const float4*>(s_vec + BN + cl0 + 4 * u);
+            const float4 be = *reinterpret_cast<const float4*>(s_vec + 2 * BN + cl0 + 4 * u);
+            x[0] = fmaf(fmaf(x[0], rstd, nmr), gg.x, be.x);
+            x[1] = fmaf(fmaf(x[1], rstd, nmr), gg.y, be.y);
+            x[2] = fmaf(fmaf(x[2], rstd, nmr), gg.z, be.z);
+            x[3] = fmaf(fmaf(x[3], rstd, nmr), gg.w, be.w);
+          }
+          float4* slot = reinterpret_cast<float4*>(f32 + lane * 32 + ((u ^ sw128) << 2));
+          if constexpr (RES == 2) {
+            const float4 rr = *slot;
+            x[0] += rr.x;
+            x[1] += rr.y;
+            x[2] += rr.z;
+            x[3] += rr.w;
+          }
+          v[4 * u] = x[0];
+          v[4 * u + 1] = x[1];
+          v[4 * u + 2] = x[2];
+          v[4 * u + 3] = x[3];
+          if (e.o32 || e.o32b) *slot = make_float4(x[0], x[1], x[2], x[3]);
+        }
+        if (e.o16) {
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            __half2 h0 = __floats2half2_rn(v[8 * u], v[8 * u + 1]);
+            __half2 h1 = __floats2half2_rn(v[8 * u + 2], v[8 * u + 3]);
+            __half2 h2 = __floats2half2_rn(v[8 * u + 4], v[8 * u + 5]);
+            __half2 h3 = __floats2half2_rn(v[8 * u + 6], v[8 * u + 7]);
+            *reinterpret_cast<uint4*>(f16 + lane * 64 + ((u ^ sw64) << 4)) =
+                make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                           *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (e.o32) box_store(&om.o32, f32, n0 + cl0);
+          if (e.o32b) box_store(&om.o32b, f32, n0 + cl0);
+          if (e.o16) box_store(&om.o16, f16, n0 + cl0);
+          bulk_commit();
+        }
+      }
+    } else if constexpr (STORE == STORE_SHUFFLE2) {
       float mean = 0.0f, rstd = 1.0f;
       if constexpr (LN) {
         float s1 = 0.0f, s2 = 0.0f;
@@ -284,39 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           val[it] = *reinterpret_cast<const float4*>(stg + rr * 36 + cg * 4);
           src[it] = s_row[(wrow0 + rr) * 4];
         }
-        if constexpr (STORE == STORE_ROWS) {
-          if constexpr (RES == 2) {
-            float4 rp[8];
-#pragma unroll
-            for (int it = 0; it < 8; it++)
-              rp[it] = src[it] >= 0 ? __ldg(reinterpret_cast<const float4*>(
-                                          e.res_post + (size_t)src[it] * e.ld_res_post + col))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int it = 0; it < 8; it++) {
-              val[it].x += rp[it].x;
-              val[it].y += rp[it].y;
-              val[it].z += rp[it].z;
-              val[it].w += rp[it].w;
-            }
-          }
-#pragma unroll
-          for (int it = 0; it < 8; it++) {
-            if (src[it] < 0) continue;
-            const int4 rw = *reinterpret_cast<const int4*>(s_row + (wrow0 + it * 4 + sub) * 4);
-            if (e.o32) *reinterpret_cast<float4*>(e.o32 + (size_t)rw.y * e.ld32 + col) = val[it];
-            if (e.o32b)
-              *reinterpret_cast<float4*>(e.o32b + (size_t)rw.w * e.ld32b + col) = val[it];
-            if (e.o16) {
-              __half2 h0 = __floats2half2_rn(val[it].x, val[it].y);
-              __half2 h1 = __floats2half2_rn(val[it].z, val[it].w);
-              uint2 u;
-              u.x = *reinterpret_cast<uint32_t*>(&h0);
-              u.y = *reinterpret_cast<uint32_t*>(&h1);
-              *reinterpret_cast<uint2*>(e.o16 + (size_t)rw.z * e.ld16 + col) = u;
-            }
-          }
-        } else {
+        {
           const int qd = col / F, f = col - qd * F;
           const int dy = qd >> 1, dx = qd & 1;
           size_t dst[8];
@@ -393,6 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (warp >= 2 && lane == 0) bulk_wait<0>();  // this warp's bulk stores are performed
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -402,11 +497,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE>
-cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& a,
-                     cudaStream_t st) {
-  const size_t smem = 1024 + (size_t)STAGES * (128 * 128 + BN * 128) +
-                      kEpiWarps * kStageFloats * 4 + 3 * BN * 4 + kEpiWarps * 32 * 4 * 4 +
-                      (2 * STAGES + 5) * 8 + 16;
+cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const OutMaps& om,
+                     const GemmArgs& a, cudaStream_t st) {
+  const size_t smem = 1024 + (size_t)STAGES * (128 * 128 + BN * 128) + kEpiWarps * kWarpBuf +
+                      3 * BN * 4 + kEpiWarps * 32 * 4 * 4 + (2 * STAGES + 5 + 2 * kEpiWarps) * 8 +
+                      16;
   static int ctas = 0;  // resident CTAs per device (SMs x CTAs per SM), one process per GPU
   if (ctas == 0) {
     cudaError_t err = cudaFuncSetAttribute(k_gemm<BN, STAGES, ACT, LN, RES, STORE>,
@@ -426,7 +521,7 @@ cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const Gem
   long G = tiles < ctas ? tiles : ctas;
   G = (G / NT) * NT;
   if (G < NT) G = NT;
-  k_gemm<BN, STAGES, ACT, LN, RES, STORE><<<(unsigned)G, kThreads, smem, st>>>(mapA, mapB, a);
+  k_gemm<BN, STAGES, ACT, LN, RES, STORE><<<(unsigned)G, kThreads, smem, st>>>(mapA, mapB, om, a);
   return cudaGetLastError();
 }
 
@@ -435,10 +530,10 @@ cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const Gem
 // The epilogue variants the forward pass uses, per N tile.
 #define S2S_VARIANT(BN_, ST_, ACT_, LN_, RES_, STORE_)                                 \
   if (BN == BN_ && act == ACT_ && ln == LN_ && res == RES_ && store == STORE_)        \
-    return launch_t<BN_, ST_, ACT_, LN_, RES_, STORE_>(mapA, mapB, a, st);
+    return launch_t<BN_, ST_, ACT_, LN_, RES_, STORE_>(mapA, mapB, om, a, st);
 
-cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& a,
-                        int BN, cudaStream_t st) {
+cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const OutMaps& om,
+                        const GemmArgs& a, int BN, cudaStream_t st) {
   if (a.N % BN != 0 || (a.conv == 0 && a.K % 64 != 0)) return cudaErrorInvalidValue;
   const Epi& e = a.epi;
   if (e.ln_n > 0 && a.N != BN) return cudaErrorInvalidValue;
@@ -448,30 +543,30 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   const int res = e.res_pre ? 1 : (e.res_post ? 2 : 0);
   const int store = e.store;
   // embed 180 (Cp 192): QKV, convs, fc1, proj/fc2, patch_embed, stage tail, body skip
-  S2S_VARIANT(192, 4, ACT_NONE, false, 0, STORE_ROWS)
-  S2S_VARIANT(192, 4, ACT_GELU, false, 0, STORE_ROWS)
-  S2S_VARIANT(192, 4, ACT_NONE, true, 2, STORE_ROWS)
-  S2S_VARIANT(192, 4, ACT_NONE, true, 0, STORE_ROWS)
-  S2S_VARIANT(192, 4, ACT_NONE, false, 1, STORE_ROWS)
-  S2S_VARIANT(192, 4, ACT_NONE, true, 1, STORE_ROWS)
-  S2S_VARIANT(192, 4, ACT_NONE, false, 2, STORE_ROWS)
+  S2S_VARIANT(192, 3, ACT_NONE, false, 0, STORE_ROWS)
+  S2S_VARIANT(192, 3, ACT_GELU, false, 0, STORE_ROWS)
+  S2S_VARIANT(192, 3, ACT_NONE, true, 2, STORE_ROWS)
+  S2S_VARIANT(192, 3, ACT_NONE, true, 0, STORE_ROWS)
+  S2S_VARIANT(192, 3, ACT_NONE, false, 1, STORE_ROWS)
+  S2S_VARIANT(192, 3, ACT_NONE, true, 1, STORE_ROWS)
+  S2S_VARIANT(192, 3, ACT_NONE, false, 2, STORE_ROWS)
   // embed 60 (Cp 64) and the 64-channel head convs
-  S2S_VARIANT(64, 6, ACT_NONE, false, 0, STORE_ROWS)
-  S2S_VARIANT(64, 6, ACT_NONE, true, 2, STORE_ROWS)
-  S2S_VARIANT(64, 6, ACT_NONE, true, 0, STORE_ROWS)
-  S2S_VARIANT(64, 6, ACT_NONE, false, 1, STORE_ROWS)
-  S2S_VARIANT(64, 6, ACT_NONE, true, 1, STORE_ROWS)
-  S2S_VARIANT(64, 6, ACT_NONE, false, 2, STORE_ROWS)
-  S2S_VARIANT(64, 6, ACT_LRELU, false, 0, STORE_ROWS)
-  S2S_VARIANT(96, 6, ACT_NONE, false, 0, STORE_ROWS)
-  S2S_VARIANT(128, 4, ACT_GELU, false, 0, STORE_ROWS)
+  S2S_VARIANT(64, 4, ACT_NONE, false, 0, STORE_ROWS)
+  S2S_VARIANT(64, 4, ACT_NONE, true, 2, STORE_ROWS)
+  S2S_VARIANT(64, 4, ACT_NONE, true, 0, STORE_ROWS)
+  S2S_VARIANT(64, 4, ACT_NONE, false, 1, STORE_ROWS)
+  S2S_VARIANT(64, 4, ACT_NONE, true, 1, STORE_ROWS)
+  S2S_VARIANT(64, 4, ACT_NONE, false, 2, STORE_ROWS)
+  S2S_VARIANT(64, 4, ACT_LRELU, false, 0, STORE_ROWS)
+  S2S_VARIANT(96, 4, ACT_NONE, false, 0, STORE_ROWS)
+  S2S_VARIANT(128, 3, ACT_GELU, false, 0, STORE_ROWS)
   // x2 octave convs with the pixel-shuffle store (+ the compressed head's bicubic add)
-  S2S_VARIANT(256, 3, ACT_NONE, false, 0, STORE_SHUFFLE2)
-  S2S_VARIANT(256, 3, ACT_NONE, false, 2, STORE_SHUFFLE2)
+  S2S_VARIANT(256, 2, ACT_NONE, false, 0, STORE_SHUFFLE2)
+  S2S_VARIANT(256, 2, ACT_NONE, false, 2, STORE_SHUFFLE2)
   // 3-channel outputs
-  S2S_VARIANT(32, 6, ACT_NONE, false, 0, STORE_PLANES)
-  S2S_VARIANT(32, 6, ACT_NONE, false, 0, STORE_DIRECT)
-  S2S_VARIANT(64, 6, ACT_NONE, false, 0, STORE_DIRECT)
+  S2S_VARIANT(32, 4, ACT_NONE, false, 0, STORE_PLANES)
+  S2S_VARIANT(32, 4, ACT_NONE, false, 0, STORE_DIRECT)
+  S2S_VARIANT(64, 4, ACT_NONE, false, 0, STORE_DIRECT)
   return cudaErrorNotSupported;
 }
 #undef S2S_VARIANT
@@ -522,6 +617,38 @@ bool make_map_nhwc(CUtensorMap* m, const void* base, int B, int H, int W, int Cp
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box,
             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_map_out_rows(CUtensorMap* m, const void* base, int elem_bytes, uint64_t rows,
+                       uint64_t ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (ld * elem_bytes) % 16 != 0 || (reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return false;
+  cuuint64_t dims[2] = {ld, rows};
+  cuuint64_t strides[1] = {ld * elem_bytes};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+            2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            elem_bytes == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_map_out_nhwc(CUtensorMap* m, const void* base, int elem_bytes, int B, int H, int W,
+                       int ld, int boxw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (ld * elem_bytes) % 16 != 0 || (reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return false;
+  const int bw = boxw < 32 ? boxw : 32, bh = 32 / bw;
+  cuuint64_t dims[4] = {(cuuint64_t)ld, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)ld * elem_bytes, (cuuint64_t)W * ld * elem_bytes,
+                           (cuuint64_t)H * W * ld * elem_bytes};
+  cuuint32_t box[4] = {32, (cuuint32_t)bw, (cuuint32_t)bh, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return fn(m, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+            4, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            elem_bytes == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 void conv_box(int W, int* boxw, int* boxh) {

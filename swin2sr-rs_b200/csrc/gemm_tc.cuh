@@ -11,7 +11,7 @@ enum Act : int { ACT_NONE = 0, ACT_GELU = 1, ACT_LRELU = 2 };
 
 // Where the epilogue writes.
 enum Store : int {
-  STORE_ROWS = 0,      // row-major rows (optionally through a row map), fp32 and/or fp16
+  STORE_ROWS = 0,      // row-major rows (image order), fp32 and/or fp16, by TMA bulk stores
   STORE_SHUFFLE2 = 1,  // conv output pixel-shuffled by 2 into an NHWC fp16 plane (columns
                        // ordered (dy, dx, f)), optional fp32 residual at the destination
   STORE_PLANES = 2,    // first 3 columns -> NCHW fp32 planes: denormalised+cropped and/or raw
@@ -31,22 +31,20 @@ struct Epi {
   const float* ln_b;
   int ln_n;
   float ln_eps;
-  // fp32 residual added last (STORE_ROWS: at the logical row; STORE_SHUFFLE2: at
-  // the destination pixel).
+  // fp32 residual added last (STORE_ROWS: at the logical row, brought in by TMA
+  // through OutMaps::res; STORE_SHUFFLE2: at the destination pixel).
   const float* res_post;
   int ld_res_post;
-  // Columns [n_valid, N) are written as zero.
+  // Columns [n_valid, N) hold zeros (padded weights, bias and norms make them so).
   int n_valid;
-  // Outputs (STORE_ROWS / STORE_SHUFFLE2).
+  // Outputs. STORE_ROWS writes them through OutMaps (o32, o32b, o16); the pointers
+  // say which are present. STORE_SHUFFLE2 writes o16 directly.
   float* o32;
   int ld32;
-  const int* map32;
   float* o32b;
   int ld32b;
-  const int* map32b;
   __half* o16;
   int ld16;
-  const int* map16;
   int store;
   // STORE_PLANES / STORE_DIRECT
   float* planes;      // denormalised, cropped to crop_h x crop_w (x scale for DIRECT)
@@ -65,10 +63,17 @@ struct GemmArgs {
   Epi epi;
 };
 
+// TMA descriptors of the STORE_ROWS outputs and of the post-norm residual: 32x32
+// boxes (fp32 with the 128-byte swizzle, fp16 with the 64-byte swizzle), 2-D over
+// [M][ld] rows in GEMM mode, 4-D over [B][H][W][ld] in conv mode (make_map_out_*).
+struct OutMaps {
+  CUtensorMap o32, o32b, o16, res;
+};
+
 // Launch D = A * B^T (+ epilogue). mapA / mapB are TMA descriptors built by
 // make_map_* below. BN is the N tile (<= 256, multiple of 32).
-cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const GemmArgs& a,
-                        int BN, cudaStream_t st);
+cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const OutMaps& om,
+                        const GemmArgs& a, int BN, cudaStream_t st);
 
 // Fused MLP sublayer (csrc/mlp.cu): X <- X + LN(fc2(GELU(fc1(X16)))) in place.
 struct MlpArgs {
@@ -94,6 +99,14 @@ bool make_map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t col
                    uint32_t box_rows);
 bool make_map_nhwc(CUtensorMap* m, const void* base, int B, int H, int W, int Cp, int boxw,
                    int boxh);
+
+// Output / residual maps (32-column boxes): rows [rows][ld] in GEMM mode, or the
+// NHWC plane [B][H][W][ld] with the 32-row sub-box a warp of a conv tile owns
+// (boxw = the conv tile width). elem_bytes 4 (fp32) or 2 (fp16).
+bool make_map_out_rows(CUtensorMap* m, const void* base, int elem_bytes, uint64_t rows,
+                       uint64_t ld);
+bool make_map_out_nhwc(CUtensorMap* m, const void* base, int elem_bytes, int B, int H, int W,
+                       int ld, int boxw);
 
 // The M tile of a convolution over a W-wide plane: box width = the largest power
 // of two <= 128 dividing W.
