@@ -684,7 +684,13 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         m.x = P->X;
         m.x16 = P->X16;
         L.run("mlp_fused", [&] {
-          return launch_mlp(P->mX16, bl.fc1.map, bl.fc2.map, m, Cp, H->HIDp, st);
+          Epi eo = epi0();
+          eo.o32 = P->X;
+          eo.ld32 = Cp;
+          eo.o16 = P->X16;
+          eo.ld16 = Cp;
+          const OutMaps om = out_maps(P, gemm_args(M, Cp, Cp, eo));
+          return launch_mlp(P->mX16, bl.fc1.map, bl.fc2.map, om.o32, om.o16, m, Cp, H->HIDp, st);
         });
       } else {
         {  // fc1 + GELU
@@ -729,8 +735,15 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       Epi e = epi0();
       e.bias = stg.pe.b;
       e.n_valid = C;
-      e.res_pre = P->S;
-      e.ld_res_pre = Cp;
+      // the stage residual: without a norm it is added after the bias (TMA path); the
+      // last stage's final LayerNorm normalises the sum, so there it comes first
+      if (last) {
+        e.res_pre = P->S;
+        e.ld_res_pre = Cp;
+      } else {
+        e.res_post = P->S;
+        e.ld_res_post = Cp;
+      }
       if (!last) {
         e.o32 = P->X;
         e.ld32 = Cp;

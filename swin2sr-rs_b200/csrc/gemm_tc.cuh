@@ -89,9 +89,11 @@ struct MlpArgs {
 };
 
 // mapX: rows map of x16 (box 128 rows); mapW1: fc1 weight [HP][CP] (box N1 rows);
-// mapW2: fc2 weight [CP][HP] (box CP rows). Supported (cp, hp): (192, 384), (64, 128).
+// mapW2: fc2 weight [CP][HP] (box CP rows); mapX32 / mapX16o: make_map_out_rows maps of
+// x (fp32, also the residual) and x16. Supported (cp, hp): (192, 384), (64, 128).
 cudaError_t launch_mlp(const CUtensorMap& mapX, const CUtensorMap& mapW1,
-                       const CUtensorMap& mapW2, const MlpArgs& a, int cp, int hp,
+                       const CUtensorMap& mapW2, const CUtensorMap& mapX32,
+                       const CUtensorMap& mapX16o, const MlpArgs& a, int cp, int hp,
                        cudaStream_t st);
 
 // TMA descriptor helpers (driver entry point resolved at first use).

@@ -21,7 +21,10 @@ namespace {
 
 constexpr int kMlpThreads = 320;
 constexpr int kMlpEpiWarps = 8;
-constexpr int kMlpStage = 32 * 36;
+// Epilogue-2 tiles per warp: two fp32 32x32 tiles (residual in, result out, 128-byte
+// swizzle) in a dedicated region, and two fp16 tiles (64-byte swizzle) placed in the
+// hidden-head buffer, which is dead between fc2 and the next tile's epilogue 1.
+constexpr int kMlpF32Buf = 2 * 4096;
 
 template <int CP, int HP, int N1, int STAGES>
 struct MlpCfg {
@@ -33,16 +36,17 @@ struct MlpCfg {
   static constexpr int SLOT_ROWS = N1 > CP ? N1 : CP;
   static constexpr int SLOT = SLOT_ROWS * 128;        // ring slot bytes
   static constexpr uint32_t TCOLS = HP <= 32 ? 32 : HP <= 64 ? 64 : HP <= 128 ? 128 : HP <= 256 ? 256 : 512;
-  static constexpr size_t SMEM = 1024 + (size_t)KC1 * 16384 + (size_t)NH0 * 16384 +
-                                 (size_t)STAGES * SLOT + kMlpEpiWarps * kMlpStage * 4 +
-                                 (HP + 3 * CP) * 4 + kMlpEpiWarps * 32 * 4 * 4 +
-                                 (2 * STAGES + 2 * NP1 + 8) * 8 + 16;
+  static constexpr int H0B = NH0 * 16384 > kMlpEpiWarps * 4096 ? NH0 * 16384 : kMlpEpiWarps * 4096;
+  static constexpr size_t SMEM = 1024 + (size_t)KC1 * 16384 + (size_t)H0B + (size_t)STAGES * SLOT +
+                                 kMlpEpiWarps * kMlpF32Buf + (HP + 3 * CP) * 4 +
+                                 (2 * STAGES + 2 * NP1 + 9 + 2 * kMlpEpiWarps) * 8 + 16;
 };
 
 template <int CP, int HP, int N1, int STAGES>
 __global__ void __launch_bounds__(kMlpThreads, 1)
     k_mlp(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapW1,
-          const __grid_constant__ CUtensorMap mapW2, const MlpArgs a) {
+          const __grid_constant__ CUtensorMap mapW2, const __grid_constant__ CUtensorMap mapX32,
+          const __grid_constant__ CUtensorMap mapX16o, const MlpArgs a) {
   using Cfg = MlpCfg<CP, HP, N1, STAGES>;
   constexpr int KC1 = Cfg::KC1, KC2 = Cfg::KC2, NP1 = Cfg::NP1, NH0 = Cfg::NH0;
   static_assert(NH0 >= 0, "hidden must be at least as wide as the embedding");
@@ -52,12 +56,11 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sX = smem;                           // KC1 chunks: X16 tile, then hidden tail
-  uint8_t* sH0 = sX + KC1 * 16384;              // NH0 chunks: hidden head
-  uint8_t* ring = sH0 + NH0 * 16384;
-  float* stage = reinterpret_cast<float*>(ring + STAGES * Cfg::SLOT);
-  float* s_vec = stage + kMlpEpiWarps * kMlpStage;  // b1[HP], b2[CP], g2[CP], beta2[CP]
-  int* s_rows = reinterpret_cast<int*>(s_vec + HP + 3 * CP);
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_rows + kMlpEpiWarps * 32 * 4);
+  uint8_t* sH0 = sX + KC1 * 16384;              // NH0 chunks: hidden head / epilogue-2 fp16 tiles
+  uint8_t* ring = sH0 + Cfg::H0B;
+  uint8_t* f32buf = ring + STAGES * Cfg::SLOT;  // [kMlpEpiWarps][2][4096]
+  float* s_vec = reinterpret_cast<float*>(f32buf + kMlpEpiWarps * kMlpF32Buf);  // b1, b2, g2, beta2
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_vec + HP + 3 * CP);
   uint64_t* empty = full + STAGES;
   uint64_t* acc1 = empty + STAGES;   // [NP1] fc1 part ready
   uint64_t* hfull = acc1 + NP1;      // [NP1] hidden part written (8 warp arrivals)
@@ -66,7 +69,9 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   uint64_t* acc2 = xfree + 1;        // fc2 ready
   uint64_t* d2free = acc2 + 1;       // epilogue-2 drained D2 (8 warp arrivals)
   uint64_t* fin = d2free + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(fin + 1);
+  uint64_t* rbar = fin + 1;          // [kMlpEpiWarps][2] residual tile landed
+  uint64_t* hfree = rbar + 2 * kMlpEpiWarps;  // epilogue-2 fp16 tiles read out (8 warp arrivals)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(hfree + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_tiles = (a.M + 127) / 128;
@@ -89,6 +94,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     mbar_init(acc2, 1);
     mbar_init(d2free, kMlpEpiWarps);
     mbar_init(fin, 1);
+    for (int k = 0; k < 2 * kMlpEpiWarps; k++) mbar_init(&rbar[k], 1);
+    mbar_init(hfree, kMlpEpiWarps);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -191,7 +198,6 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     const int half = (warp - 2) >> 2;
     const int et = threadIdx.x - 64;
     const int r = q * 32 + lane;  // tile row of this thread in the thread-per-row phases
-    int* s_row = s_rows + (warp - 2) * 32 * 4 - q * 32 * 4;
     for (int c = et; c < HP; c += 32 * kMlpEpiWarps) s_vec[c] = a.b1[c];
     for (int c = et; c < CP; c += 32 * kMlpEpiWarps) {
       s_vec[HP + c] = a.b2[c];
@@ -199,16 +205,19 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       s_vec[HP + 2 * CP + c] = a.beta2[c];
     }
     asm volatile("bar.sync 1, %0;" ::"r"(32 * kMlpEpiWarps) : "memory");
-    float* stg = stage + (warp - 2) * kMlpStage;
+    const int wq = warp - 2;
+    uint8_t* wf32 = f32buf + wq * kMlpF32Buf;
+    uint8_t* wf16 = sH0 + wq * 4096;
+    uint64_t* wrb = rbar + 2 * wq;
+    uint32_t jcnt = 0;
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     int i = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
-      const int m = t * 128 + r;
-      const bool valid = m < a.M;
-      s_row[r * 4] = valid ? m : -1;
-      __syncwarp();
+      const int row0 = t * 128 + q * 32;  // this warp's 32 rows as a TMA box origin
       // ---- epilogue 1: hidden = GELU(D1 + b1) -> fp16 -> shared (fc2's A operand)
+      // the hidden-head buffer held the previous tile's epilogue-2 fp16 tiles
+      if (i > 0 && !mbar_wait(hfree, (i - 1) & 1, DEV_TIMEOUT_ACC)) break;
       for (int p = 0; p < NP1; p++) {
         if (!mbar_wait(&acc1[p], i & 1, DEV_TIMEOUT_ACC)) {
           ok = false;
@@ -246,7 +255,13 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         if (lane == 0) mbar_arrive(&hfull[p]);
       }
       if (!ok) break;
-      // ---- epilogue 2: X <- X + LN2(D2 + b2), X16 <- fp16(X)
+      // ---- epilogue 2: X <- X + LN2(D2 + b2), X16 <- fp16(X), through TMA
+      // the first residual tile is requested before waiting for fc2
+      if (lane == 0 && half < CP / 32) {
+        bulk_wait_read<0>();
+        mbar_arrive_expect_tx(&wrb[jcnt & 1], 4096);
+        tma_load_2d(wf32 + (jcnt & 1) * 4096, &mapX32, &wrb[jcnt & 1], half * 32, row0);
+      }
       if (!mbar_wait(acc2, i & 1, DEV_TIMEOUT_ACC)) break;
       tc_fence_after();
       float s1 = 0.0f, s2 = 0.0f;
@@ -264,57 +279,74 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       const float nf = (float)a.ln_n;
       const float mean = s1 / nf;
       const float rstd = 1.0f / sqrtf(fmaxf(s2 / nf - mean * mean, 0.0f) + a.ln_eps);
-      const int sub = lane >> 3, cg = lane & 7, wrow0 = q * 32;
+      const float nmr = -mean * rstd;
+      const int sw128 = lane & 7, sw64 = (lane >> 1) & 3;
 #pragma unroll 1
-      for (int c = half; c < CP / 32; c += 2) {
+      for (int c = half; c < CP / 32; c += 2, jcnt++) {
+        const int jb = jcnt & 1;
+        float* f32 = reinterpret_cast<float*>(wf32 + jb * 4096);
+        uint8_t* f16 = wf16 + jb * 2048;
         float v[32];
         tmem_ld32(tq + (uint32_t)(Cfg::D2OFF + c * 32), v);
+        if (lane == 0 && c + 2 < CP / 32) {
+          bulk_wait_read<0>();
+          mbar_arrive_expect_tx(&wrb[jb ^ 1], 4096);
+          tma_load_2d(wf32 + (jb ^ 1) * 4096, &mapX32, &wrb[jb ^ 1], (c + 2) * 32, row0);
+        }
+        if (!mbar_wait(&wrb[jb], (jcnt >> 1) & 1, DEV_TIMEOUT_FULL)) {
+          ok = false;
+          break;
+        }
         const int cl0 = c * 32;
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
-          const float x = v[j] + s_vec[HP + cl0 + j];
-          v[j] = (x - mean) * rstd * s_vec[HP + CP + cl0 + j] + s_vec[HP + 2 * CP + cl0 + j];
+        for (int u = 0; u < 8; u++) {
+          const float4 bb = *reinterpret_cast<const float4*>(s_vec + HP + cl0 + 4 * u);
+          const float4 gg = *reinterpret_cast<const float4*>(s_vec + HP + CP + cl0 + 4 * u);
+          const float4 be = *reinterpret_cast<const float4*>(s_vec + HP + 2 * CP + cl0 + 4 * u);
+          float4* slot = reinterpret_cast<float4*>(f32 + lane * 32 + ((u ^ sw128) << 2));
+          const float4 rr = *slot;
+          float4 o;
+          o.x = fmaf(fmaf(v[4 * u] + bb.x, rstd, nmr), gg.x, be.x) + rr.x;
+          o.y = fmaf(fmaf(v[4 * u + 1] + bb.y, rstd, nmr), gg.y, be.y) + rr.y;
+          o.z = fmaf(fmaf(v[4 * u + 2] + bb.z, rstd, nmr), gg.z, be.z) + rr.z;
+          o.w = fmaf(fmaf(v[4 * u + 3] + bb.w, rstd, nmr), gg.w, be.w) + rr.w;
+          *slot = o;
+          v[4 * u] = o.x;
+          v[4 * u + 1] = o.y;
+          v[4 * u + 2] = o.z;
+          v[4 * u + 3] = o.w;
         }
-        float4* srow = reinterpret_cast<float4*>(stg + lane * 36);
 #pragma unroll
-        for (int j = 0; j < 8; j++)
-          srow[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        for (int u = 0; u < 4; u++) {
+          __half2 h0 = __floats2half2_rn(v[8 * u], v[8 * u + 1]);
+          __half2 h1 = __floats2half2_rn(v[8 * u + 2], v[8 * u + 3]);
+          __half2 h2 = __floats2half2_rn(v[8 * u + 4], v[8 * u + 5]);
+          __half2 h3 = __floats2half2_rn(v[8 * u + 6], v[8 * u + 7]);
+          *reinterpret_cast<uint4*>(f16 + lane * 64 + ((u ^ sw64) << 4)) =
+              make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                         *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+        }
+        fence_proxy_async_smem();
         __syncwarp();
-        const int col = cl0 + cg * 4;
-        float4 val[8], rp[8];
-        int src[8];
-#pragma unroll
-        for (int it = 0; it < 8; it++) {
-          const int rr = it * 4 + sub;
-          val[it] = *reinterpret_cast<const float4*>(stg + rr * 36 + cg * 4);
-          src[it] = s_row[(wrow0 + rr) * 4];
+        if (lane == 0) {
+          tma_store_2d(&mapX32, f32, cl0, row0);
+          tma_store_2d(&mapX16o, f16, cl0, row0);
+          bulk_commit();
         }
-#pragma unroll
-        for (int it = 0; it < 8; it++)
-          rp[it] = src[it] >= 0 ? *reinterpret_cast<const float4*>(a.x + (size_t)src[it] * CP + col)
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int it = 0; it < 8; it++) {
-          if (src[it] < 0) continue;
-          float4 o = val[it];
-          o.x += rp[it].x;
-          o.y += rp[it].y;
-          o.z += rp[it].z;
-          o.w += rp[it].w;
-          *reinterpret_cast<float4*>(a.x + (size_t)src[it] * CP + col) = o;
-          __half2 h0 = __floats2half2_rn(o.x, o.y);
-          __half2 h1 = __floats2half2_rn(o.z, o.w);
-          uint2 u;
-          u.x = *reinterpret_cast<uint32_t*>(&h0);
-          u.y = *reinterpret_cast<uint32_t*>(&h1);
-          *reinterpret_cast<uint2*>(a.x16 + (size_t)src[it] * CP + col) = u;
-        }
-        __syncwarp();
       }
+      if (!ok) break;
+      // the fp16 tiles live in the hidden-head buffer: every warp's stores must have
+      // read them before the next tile's epilogue 1 writes there
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(d2free);
+      if (lane == 0) {
+        mbar_arrive(d2free);
+        mbar_arrive(hfree);
+      }
     }
+    if (lane == 0) bulk_wait<0>();
   }
 
   tc_fence_before();
@@ -327,7 +359,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
 
 template <int CP, int HP, int N1, int STAGES>
 cudaError_t launch_mlp_t(const CUtensorMap& mX, const CUtensorMap& mW1, const CUtensorMap& mW2,
-                         const MlpArgs& a, cudaStream_t st) {
+                         const CUtensorMap& mX32, const CUtensorMap& mX16o, const MlpArgs& a,
+                         cudaStream_t st) {
   using Cfg = MlpCfg<CP, HP, N1, STAGES>;
   static int ctas = 0;
   if (ctas == 0) {
@@ -346,16 +379,19 @@ cudaError_t launch_mlp_t(const CUtensorMap& mX, const CUtensorMap& mW1, const CU
   }
   const int tiles = (a.M + 127) / 128;
   const int G = tiles < ctas ? tiles : ctas;
-  k_mlp<CP, HP, N1, STAGES><<<G, kMlpThreads, Cfg::SMEM, st>>>(mX, mW1, mW2, a);
+  k_mlp<CP, HP, N1, STAGES><<<G, kMlpThreads, Cfg::SMEM, st>>>(mX, mW1, mW2, mX32, mX16o, a);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_mlp(const CUtensorMap& mX, const CUtensorMap& mW1, const CUtensorMap& mW2,
-                       const MlpArgs& a, int cp, int hp, cudaStream_t st) {
-  if (cp == 192 && hp == 384) return launch_mlp_t<192, 384, 192, 3>(mX, mW1, mW2, a, st);
-  if (cp == 64 && hp == 128) return launch_mlp_t<64, 128, 128, 4>(mX, mW1, mW2, a, st);
+                       const CUtensorMap& mX32, const CUtensorMap& mX16o, const MlpArgs& a, int cp,
+                       int hp, cudaStream_t st) {
+  if (cp == 192 && hp == 384)
+    return launch_mlp_t<192, 384, 192, 2>(mX, mW1, mW2, mX32, mX16o, a, st);
+  if (cp == 64 && hp == 128)
+    return launch_mlp_t<64, 128, 128, 4>(mX, mW1, mW2, mX32, mX16o, a, st);
   return cudaErrorNotSupported;
 }
 
