@@ -147,6 +147,33 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- GELU
+// erf-form GELU, 0.5 x (1 + erf(x / sqrt 2)) (nn.GELU's default; the reference's
+// src/cpu.rs:1125-1132), with erf from Abramowitz & Stegun (1964), formula 7.1.28:
+//   erf(t) = 1 - (1 + a1 t + ... + a6 t^6)^-16,  t >= 0,  |error| <= 3e-7,
+// odd-extended. Branch-free: GELU = x - 0.5 x r for x >= 0 and 0.5 x r otherwise,
+// r = (1 + ...)^-16 = erfc(|x| / sqrt 2). Against the exact function it is within
+// 7e-7 absolute on [-12, 12] in fp32 (tests/test_host.py), well below the fp16
+// rounding of the hidden activations it feeds.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float t = fabsf(x) * 0.70710678118654752440f;
+  float p = 0.0000430638f;
+  p = fmaf(p, t, 0.0002765672f);
+  p = fmaf(p, t, 0.0001520143f);
+  p = fmaf(p, t, 0.0092705272f);
+  p = fmaf(p, t, 0.0422820123f);
+  p = fmaf(p, t, 0.0705230784f);
+  p = fmaf(p, t, 1.0f);
+  p = p * p;
+  p = p * p;
+  p = p * p;
+  p = p * p;
+  float r;  // hardware reciprocal (about 1 ulp); inf -> 0 for large |x|
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(p));
+  const float h = 0.5f * x * r;
+  return x >= 0.0f ? x - h : h;
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(

@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // statistics.
     auto pre = [&](float v, int cl) {
       v += s_vec[cl];
-      if constexpr (ACT == ACT_GELU) v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+      if constexpr (ACT == ACT_GELU) v = gelu_erf(v);
       if constexpr (ACT == ACT_LRELU) v = v < 0.0f ? v * e.slope : v;
       return v;
     };
@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         v[4 * u + 3] + bb.w};
 #pragma unroll
           for (int k = 0; k < 4; k++) {
-            if constexpr (ACT == ACT_GELU) x[k] = 0.5f * x[k] * (1.0f + erff(x[k] * 0.70710678118654752440f));
+            if constexpr (ACT == ACT_GELU) x[k] = gelu_erf(x[k]);
             if constexpr (ACT == ACT_LRELU) x[k] = x[k] < 0.0f ? x[k] * e.slope : x[k];
             if constexpr (RES == 1) x[k] += rpre[cl0 + 4 * u + k];
           }

@@ -231,13 +231,12 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
           const int col0 = p * N1 + c * 32;  // hidden column of v[0]
           uint32_t hv[16];
 #pragma unroll
-          for (int j = 0; j < 16; j++) {
-            float x0 = v[2 * j] + s_vec[col0 + 2 * j];
-            float x1 = v[2 * j + 1] + s_vec[col0 + 2 * j + 1];
-            x0 = 0.5f * x0 * (1.0f + erff(x0 * 0.70710678118654752440f));
-            x1 = 0.5f * x1 * (1.0f + erff(x1 * 0.70710678118654752440f));
-            __half2 h = __floats2half2_rn(x0, x1);
-            hv[j] = *reinterpret_cast<uint32_t*>(&h);
+          for (int j = 0; j < 8; j++) {
+            const float4 bb = *reinterpret_cast<const float4*>(s_vec + col0 + 4 * j);
+            const __half2 h0 = __floats2half2_rn(gelu_erf(v[4 * j] + bb.x), gelu_erf(v[4 * j + 1] + bb.y));
+            const __half2 h1 = __floats2half2_rn(gelu_erf(v[4 * j + 2] + bb.z), gelu_erf(v[4 * j + 3] + bb.w));
+            hv[2 * j] = *reinterpret_cast<const uint32_t*>(&h0);
+            hv[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&h1);
           }
           uint8_t* chunk = hchunk(col0 >> 6);
           const int u0 = (col0 & 63) >> 3;  // first 16-byte unit in the 128-byte row

@@ -145,3 +145,24 @@ def test_workloads_are_seeded_and_in_range():
     assert 0.0 <= a.min() and a.max() <= 1.0 and a.std() > 0.05
     rw = wl.make_input("realworld-x4")
     assert rw.shape == (1, 3, 512, 512) and 0.0 <= rw.min() and rw.max() <= 1.0
+
+
+def test_gelu_erf_approximation_bound():
+    """The kernels' GELU uses Abramowitz & Stegun 7.1.28 for erf (csrc/common.cuh,
+    gelu_erf); evaluated in fp32 with the same operation order it stays within 1e-6
+    absolute of the exact erf-form GELU the reference computes (src/cpu.rs:1125-1132)."""
+    import math
+    a = np.array([0.0705230784, 0.0422820123, 0.0092705272, 0.0001520143, 0.0002765672,
+                  0.0000430638], np.float32)
+    x = np.linspace(-12, 12, 200001).astype(np.float32)
+    t = np.abs(x) * np.float32(0.70710678118654752440)
+    p = a[5]
+    for c in a[4::-1]:
+        p = p * t + c
+    p = p * t + np.float32(1.0)
+    for _ in range(4):
+        p = p * p
+    h = np.float32(0.5) * x * (np.float32(1.0) / p)
+    got = np.where(x >= 0, x - h, h).astype(np.float64)
+    ref = np.array([0.5 * float(v) * (1 + math.erf(float(v) / math.sqrt(2))) for v in x])
+    assert np.abs(got - ref).max() < 1e-6
