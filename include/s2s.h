@@ -138,6 +138,24 @@ int64_t s2s_launch_count(const s2s_handle* h);
 int s2s_debug_stop_after(s2s_handle* h, int64_t launches);
 int64_t s2s_debug_read(s2s_handle* h, const char* buffer, float* host, int64_t capacity);
 
+/* No counterpart in the reference. Window attention of block `block` of stage
+ * `stage` for callers that must not allocate: it allocates no device or host
+ * memory and needs no plan. The window -> image row table it reads (which a
+ * forward keeps in its workspace) lives in a fixed device array of the library
+ * holding S2S_NOALLOC_MAX_TOKENS rows (4 MiB); batch * hp * wp above that is
+ * rejected with S2S_ERR_INVALID. d_qkv is [batch*hp*wp][3*heads*dp] fp16 in image
+ * order, per token [head][q|k|v][dp] with dp = head_dim rounded up to 16 (16-byte
+ * aligned); d_out is [batch*hp*wp][ld_out] fp16, of which columns [0, embed) are
+ * written. hp and wp are the padded plane (multiples of the window); odd blocks
+ * use the shifted window grid. Work is enqueued on `stream` (NULL = the handle's
+ * stream) without synchronising. The first call on each device looks up the
+ * array's device address, so make it before any stream capture on that device.
+ * Each call rewrites the table before reading it (nothing has to start at zero);
+ * overlapping calls on one device race on the table. */
+#define S2S_NOALLOC_MAX_TOKENS 1048576
+int s2s_window_attention_noalloc(s2s_handle* h, int stage, int block, int batch, int hp, int wp,
+                                 const void* d_qkv, void* d_out, int ld_out, void* stream);
+
 void s2s_destroy(s2s_handle* h);
 
 const char* s2s_version(void);

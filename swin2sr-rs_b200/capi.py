@@ -25,7 +25,8 @@ UPSAMPLER_CODE = {"pixelshuffle": 0, "pixelshuffledirect": 1, "nearest+conv": 2,
 EXPORTS = ("s2s_create", "s2s_forward", "s2s_forward_batch", "s2s_forward_device",
            "s2s_aux_dims", "s2s_uploaded_bytes", "s2s_workspace_bytes", "s2s_last_error",
            "s2s_profile_enable", "s2s_profile_report", "s2s_launch_count", "s2s_destroy",
-           "s2s_version", "s2s_debug_stop_after", "s2s_debug_read")
+           "s2s_version", "s2s_debug_stop_after", "s2s_debug_read",
+           "s2s_window_attention_noalloc")
 
 
 class S2SConfig(ctypes.Structure):
@@ -91,6 +92,9 @@ def load() -> ctypes.CDLL:
     L.s2s_debug_stop_after.restype = ctypes.c_int
     L.s2s_debug_read.argtypes = [vp, ctypes.c_char_p, fp, ctypes.c_int64]
     L.s2s_debug_read.restype = ctypes.c_int64
+    L.s2s_window_attention_noalloc.argtypes = [vp] + [ctypes.c_int] * 5 + [vp, vp, ctypes.c_int,
+                                                                          vp]
+    L.s2s_window_attention_noalloc.restype = ctypes.c_int
     L.s2s_version.argtypes = []
     L.s2s_version.restype = ctypes.c_char_p
     _lib = L
@@ -205,6 +209,13 @@ class Handle:
         out = np.empty(n, np.float32)
         self.L.s2s_debug_read(self.h, name.encode(), _fp(out), n)
         return out
+
+    def window_attention_noalloc(self, stage: int, block: int, B: int, hp: int, wp: int,
+                                 d_qkv: int, d_out: int, ld_out: int, stream: int = 0):
+        """s2s_window_attention_noalloc on device pointers (enqueued, not synchronised)."""
+        self._check(self.L.s2s_window_attention_noalloc(
+            self.h, stage, block, B, hp, wp, ctypes.c_void_p(d_qkv), ctypes.c_void_p(d_out),
+            ld_out, ctypes.c_void_p(stream or None)))
 
     def launch_count(self) -> int:
         return int(self.L.s2s_launch_count(self.h))

@@ -5,3 +5,4 @@
 #include "mlp.cu"
 #include "misc.cu"
 #include "engine.cu"
+#include "noalloc.cu"
