@@ -6,8 +6,14 @@
 
 A step is one whole-image forward of the workload (default classical-x4: one
 240x320 image -> 960x1280, seeded weights and input, see workloads.py). Multi-GPU
-(torchrun, one process per GPU): every rank runs its own copy of the workload
-with no communication (replicas, weak scaling); the time is the max over ranks.
+(torchrun, one process per GPU), by --mode:
+  band      (default for single-image workloads) the image is split into
+            window-aligned row bands, one per rank, with NCCL halo exchange
+            (s2s_forward_band); total work fixed ("scaling": "strong");
+  batch     (default for batched workloads) the batch is split across ranks with
+            no communication; total work fixed;
+  replicas  every rank runs its own copy of the workload (weak scaling).
+The time is the max over ranks.
 
 Printed (rank 0, one JSON line): device-resident throughput (`value`, CUDA events
 on the launch stream, L2 flushed between steps outside the timed events), the
@@ -204,6 +210,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="classical-x4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", default="auto", choices=["auto", "band", "batch", "replicas"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -230,22 +237,45 @@ def main():
     B, h, w, s = spec["batch"], spec["h"], spec["w"], wt.scale
     win = wt.window
     hp, wp = (h // win + 1) * win, (w // win + 1) * win
+    mode = args.mode
+    if mode == "auto":
+        mode = "single" if world == 1 else ("band" if B == 1 else "batch")
+    if world == 1:
+        mode = "single"
     x = wl.make_input(args.workload)
+    if mode == "batch":
+        if B % world:
+            raise SystemExit(f"batch {B} does not split over {world} ranks")
+        bl = B // world
+        x = x[rank * bl:(rank + 1) * bl]
     xa = wl.adjust(x, wt)
+    Bl = xa.shape[0]                       # images this rank processes
     handle = capi.Handle(wt, device=local)
 
     dev = torch.device("cuda", local)
+    r0, r1 = 0, h
+    own_rows = hp
+    if mode == "band":
+        uid = [capi.band_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        handle.band_init(rank, world, uid[0])
+        r0, r1 = handle.band_rows(h)
+        w0, w1 = capi.band_partition(hp // win, world, rank)
+        own_rows = win * (w1 - w0)
     d_in = torch.from_numpy(xa).to(dev)
-    d_out = torch.empty((B, 3, h * s, w * s), dtype=torch.float32, device=dev)
-    d_aux = torch.empty((B, 3, hp, wp), dtype=torch.float32, device=dev) \
+    d_out = torch.empty((Bl, 3, max(r1 - r0, 1) * s, w * s), dtype=torch.float32, device=dev)
+    d_aux = torch.empty((Bl, 3, hp, wp), dtype=torch.float32, device=dev) \
         if wt.upsampler == "pixelshuffle_aux" else None
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
 
     def step():
-        handle.forward_device(B, h, w, d_in.data_ptr(), d_out.data_ptr(),
-                              d_aux.data_ptr() if d_aux is not None else 0, sp)
+        if mode == "band":
+            handle.forward_band_device(h, w, d_in.data_ptr(), d_out.data_ptr(), sp)
+        else:
+            handle.forward_device(Bl, h, w, d_in.data_ptr(), d_out.data_ptr(),
+                                  d_aux.data_ptr() if d_aux is not None else 0, sp)
 
     for _ in range(args.warmup):
         step()
@@ -289,19 +319,29 @@ def main():
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
     out_mpix = B * h * s * w * s / 1e6
-    value = world * out_mpix / (ms_per_step / 1e3)
+    # whole-job output per step: replicas each make the workload's output
+    job_mpix = world * out_mpix if mode == "replicas" else out_mpix
+    value = job_mpix / (ms_per_step / 1e3)
 
     # ---------------------------------------------------------------- end to end
-    pin_in = torch.empty((B, 3, h, w), dtype=torch.float32).pin_memory().numpy()
-    pin_out = torch.empty((B, 3, h * s, w * s), dtype=torch.float32).pin_memory().numpy()
+    pin_in = torch.empty((Bl, 3, h, w), dtype=torch.float32).pin_memory().numpy()
+    pin_out = torch.empty((Bl, 3, max(r1 - r0, 1) * s, w * s),
+                          dtype=torch.float32).pin_memory().numpy()
+    pin_aux = torch.empty((Bl, 3, hp, wp), dtype=torch.float32).pin_memory().numpy() \
+        if wt.upsampler == "pixelshuffle_aux" else None
     mean = np.asarray(wt.mean, np.float32)[None, :, None, None]
     e2e_steps = max(3, min(args.steps, 20))
 
     def e2e_step():
         np.subtract(x, mean, out=pin_in)          # Pre::adjust on the host
         np.multiply(pin_in, np.float32(wt.img_range), out=pin_in)
-        handle._check(handle.L.s2s_forward_batch(handle.h, B, h, w, capi._fp(pin_in),
-                                                 capi._fp(pin_out), None))
+        if mode == "band":
+            handle._check(handle.L.s2s_forward_band_host(handle.h, h, w, capi._fp(pin_in),
+                                                         capi._fp(pin_out)))
+        else:
+            handle._check(handle.L.s2s_forward_batch(
+                handle.h, Bl, h, w, capi._fp(pin_in), capi._fp(pin_out),
+                capi._fp(pin_aux) if pin_aux is not None else None))
 
     e2e_step()
     if world > 1:
@@ -314,11 +354,12 @@ def main():
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = world * out_mpix / e2e_s
+    e2e_value = job_mpix / e2e_s
 
     # ---------------------------------------------------------------- roofline
     pk_burst, pk_sus, hbm, pk_kind = peaks()
-    flops = kernel_flops(wt, B, hp, wp).get(dominant)
+    # per launch on this rank: its images, or its band's owned rows
+    flops = kernel_flops(wt, Bl, own_rows, wp).get(dominant)
     roofline = None
     if flops and dom[0] > 0:
         per_launch_s = dom[1] / dom[0] / 1e3
@@ -335,9 +376,10 @@ def main():
                     "peak_kind": f"bf16 dense burst ({pk_kind})", "traffic": traffic,
                     "flops_per_launch": flops, "launches": dom[0],
                     "avg_launch_ms": round(dom[1] / dom[0], 4)}
-    whole_flops = wt.flops_forward(hp, wp, B)
-    whole = {"tflops": round(whole_flops / (ms_per_step / 1e3) / 1e12, 2),
-             "frac_of_bf16_peak": round(whole_flops / (ms_per_step / 1e3) / 1e12 / pk_burst, 4)}
+    whole_flops = wt.flops_forward(hp, wp, B) * (world if mode == "replicas" else 1)
+    whole_tf = whole_flops / (ms_per_step / 1e3) / 1e12
+    whole = {"tflops": round(whole_tf, 2),
+             "frac_of_bf16_peak": round(whole_tf / (pk_burst * world), 4)}
 
     # ---------------------------------------------------------------- CPU baseline
     cpu = None
@@ -359,17 +401,24 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "Mpix/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "higher_is_better": True,
+            "scaling": "weak" if mode in ("single", "replicas") else "strong",
+            "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
             "config": {"workload": args.workload, "batch_per_gpu": B, "input": f"{h}x{w}",
                        "output": f"{h * s}x{w * s}", "padded_plane": f"{hp}x{wp}",
                        "weights": "seeded random init (seed 0)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "parallelism": {"single": "single", "replicas": f"replicas x{world}",
+                                       "band": f"row bands x{world} (NCCL halos)",
+                                       "batch": f"batch split x{world}"}[mode],
                        "l2": "flushed between steps (256 MB write, outside the events)",
                        "precision": "fp16 operands, fp32 accumulate/residual/norms"},
             "e2e": {"value": round(e2e_value, 3), "unit": "Mpix/s",
-                    "h2d_bytes_per_step": int(B * 3 * h * w * 4),
-                    "d2h_bytes_per_step": int(B * 3 * h * s * w * s * 4)},
+                    # summed over ranks: band ranks each upload the whole input
+                    "h2d_bytes_per_step": int((world if mode in ("band", "replicas") else 1)
+                                              * B * 3 * h * w * 4),
+                    "d2h_bytes_per_step": int((world if mode == "replicas" else 1)
+                                              * B * 3 * h * s * w * s * 4)},
             "roofline": roofline, "whole_forward": whole, "cpu_baseline": cpu,
             "gpu_launches": int(launches), "clocks": clk,
             "kernel_ms_per_step": {k: round(v[1], 4) for k, v in sorted(

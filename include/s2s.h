@@ -138,6 +138,48 @@ int64_t s2s_launch_count(const s2s_handle* h);
 int s2s_debug_stop_after(s2s_handle* h, int64_t launches);
 int64_t s2s_debug_read(s2s_handle* h, const char* buffer, float* host, int64_t capacity);
 
+/* ---- Row-band sharding of one image across GPUs. No counterpart in the
+ * reference, which runs an image on one GPU (src/gpu.rs:462-583 is the forward
+ * each band repeats). The padded plane's window rows are split into contiguous
+ * bands, one per rank (one process per GPU); each rank runs the whole network on
+ * its band and swaps halo rows with its neighbours by NCCL point-to-point: 4 rows
+ * (cyclically) before every shifted block, 1 row before every 3x3 convolution, 4
+ * rows before the head. The output equals the whole-image forward's, split by rows:
+ * rank r produces output rows [row0 * scale, row1 * scale) (s2s_band_rows). */
+#define S2S_BAND_ID_BYTES 128
+
+/* The communicator id: made on one rank, its S2S_BAND_ID_BYTES bytes handed to the
+ * others by the caller (any channel). S2S_ERR_NCCL when libnccl.so.2 is absent. */
+int s2s_band_unique_id(void* id, int cap);
+
+/* Make `h` rank `rank` of `world` bands (collective: every rank calls it with the
+ * same id). world == 1 leaves band mode. Afterwards only the s2s_forward_band*
+ * calls run forwards on `h`. S2S_ERR_UNSUPPORTED for the pixelshuffle_aux head. */
+int s2s_band_init(s2s_handle* h, int rank, int world, const void* id, int id_bytes);
+
+/* The same for `world` handles of this process (one host thread per handle runs
+ * s2s_forward_band* concurrently; halos move by device-to-device copies). */
+int s2s_band_init_local(s2s_handle** handles, int world);
+
+/* Input rows [row0, row1) of a `height`-row image whose output this rank produces. */
+int s2s_band_rows(const s2s_handle* h, int height, int* row0, int* row1);
+
+/* One image, every rank at once: d_in is the whole [3][h][w] input (device), d_out
+ * this rank's [3][(row1 - row0) * s][w * s] output rows (device); enqueued on
+ * `stream` (NULL = the handle's) without synchronising. */
+int s2s_forward_band(s2s_handle* h, int height, int width, const float* d_in, float* d_out,
+                     void* stream);
+/* Host-buffer variant (synchronous). */
+int s2s_forward_band_host(s2s_handle* h, int height, int width, const float* in, float* out);
+
+/* Host-only helpers (no device, no handle): the split of `window_rows` among
+ * `world` bands (rank's window rows [w0, w1)), and the transfers of one halo
+ * exchange of `rows` rows in issue order, 4 ints each (0 send / 1 receive, peer,
+ * first local row, rows; the band's own rows are local [8, 8 + own_rows)). The
+ * latter returns the count, or -1 for bad arguments. */
+int s2s_band_partition(int window_rows, int world, int rank, int* w0, int* w1);
+int s2s_band_halo_ops(int rank, int world, int own_rows, int rows, int cyclic, int* ops, int cap);
+
 /* No counterpart in the reference. Window attention of block `block` of stage
  * `stage` for callers that must not allocate: it allocates no device or host
  * memory and needs no plan. The window -> image row table it reads (which a

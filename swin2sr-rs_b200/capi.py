@@ -26,7 +26,10 @@ EXPORTS = ("s2s_create", "s2s_forward", "s2s_forward_batch", "s2s_forward_device
            "s2s_aux_dims", "s2s_uploaded_bytes", "s2s_workspace_bytes", "s2s_last_error",
            "s2s_profile_enable", "s2s_profile_report", "s2s_launch_count", "s2s_destroy",
            "s2s_version", "s2s_debug_stop_after", "s2s_debug_read",
-           "s2s_window_attention_noalloc")
+           "s2s_window_attention_noalloc", "s2s_band_unique_id", "s2s_band_init",
+           "s2s_band_init_local", "s2s_band_rows", "s2s_forward_band", "s2s_forward_band_host",
+           "s2s_band_partition", "s2s_band_halo_ops")
+BAND_ID_BYTES = 128
 
 
 class S2SConfig(ctypes.Structure):
@@ -95,6 +98,23 @@ def load() -> ctypes.CDLL:
     L.s2s_window_attention_noalloc.argtypes = [vp] + [ctypes.c_int] * 5 + [vp, vp, ctypes.c_int,
                                                                           vp]
     L.s2s_window_attention_noalloc.restype = ctypes.c_int
+    ip = ctypes.POINTER(ctypes.c_int)
+    L.s2s_band_unique_id.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    L.s2s_band_unique_id.restype = ctypes.c_int
+    L.s2s_band_init.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_int]
+    L.s2s_band_init.restype = ctypes.c_int
+    L.s2s_band_init_local.argtypes = [ctypes.POINTER(vp), ctypes.c_int]
+    L.s2s_band_init_local.restype = ctypes.c_int
+    L.s2s_band_rows.argtypes = [vp, ctypes.c_int, ip, ip]
+    L.s2s_band_rows.restype = ctypes.c_int
+    L.s2s_forward_band.argtypes = [vp, ctypes.c_int, ctypes.c_int, vp, vp, vp]
+    L.s2s_forward_band.restype = ctypes.c_int
+    L.s2s_forward_band_host.argtypes = [vp, ctypes.c_int, ctypes.c_int, fp, fp]
+    L.s2s_forward_band_host.restype = ctypes.c_int
+    L.s2s_band_partition.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ip, ip]
+    L.s2s_band_partition.restype = ctypes.c_int
+    L.s2s_band_halo_ops.argtypes = [ctypes.c_int] * 5 + [ip, ctypes.c_int]
+    L.s2s_band_halo_ops.restype = ctypes.c_int
     L.s2s_version.argtypes = []
     L.s2s_version.restype = ctypes.c_char_p
     _lib = L
@@ -217,5 +237,66 @@ class Handle:
             self.h, stage, block, B, hp, wp, ctypes.c_void_p(d_qkv), ctypes.c_void_p(d_out),
             ld_out, ctypes.c_void_p(stream or None)))
 
+    # ---- row-band sharding
+    def band_init(self, rank: int, world: int, uid: bytes | None = None):
+        self._check(self.L.s2s_band_init(self.h, rank, world, uid, len(uid) if uid else 0))
+
+    def band_rows(self, height: int):
+        r0, r1 = ctypes.c_int(), ctypes.c_int()
+        self._check(self.L.s2s_band_rows(self.h, height, ctypes.byref(r0), ctypes.byref(r1)))
+        return r0.value, r1.value
+
+    def forward_band(self, x_chw: np.ndarray) -> np.ndarray:
+        """This rank's output rows of one [3][h][w] image (synchronous, host buffers)."""
+        x = np.ascontiguousarray(x_chw, dtype=np.float32)
+        _, h, w = x.shape
+        r0, r1 = self.band_rows(h)
+        s = self.wt.scale
+        out = np.empty((3, (r1 - r0) * s, w * s), np.float32)
+        self._check(self.L.s2s_forward_band_host(self.h, h, w, _fp(x), _fp(out)))
+        return out
+
+    def forward_band_device(self, h: int, w: int, d_in: int, d_out: int, stream: int = 0):
+        self._check(self.L.s2s_forward_band(self.h, h, w, ctypes.c_void_p(d_in),
+                                            ctypes.c_void_p(d_out), ctypes.c_void_p(stream or None)))
+
     def launch_count(self) -> int:
         return int(self.L.s2s_launch_count(self.h))
+
+
+def band_unique_id() -> bytes:
+    """s2s_band_unique_id: the NCCL id one rank makes and hands to the others."""
+    L = load()
+    buf = ctypes.create_string_buffer(BAND_ID_BYTES)
+    rc = L.s2s_band_unique_id(buf, BAND_ID_BYTES)
+    if rc != S2S_OK:
+        raise S2SError(rc, L.s2s_last_error(None).decode())
+    return buf.raw
+
+
+def band_init_local(handles) -> None:
+    """s2s_band_init_local: `handles` become the bands of one in-process group."""
+    L = load()
+    arr = (ctypes.c_void_p * len(handles))(*[h.h.value for h in handles])
+    rc = L.s2s_band_init_local(arr, len(handles))
+    if rc != S2S_OK:
+        raise S2SError(rc, handles[0].L.s2s_last_error(handles[0].h).decode())
+
+
+def band_partition(window_rows: int, world: int, rank: int):
+    L = load()
+    a, b = ctypes.c_int(), ctypes.c_int()
+    rc = L.s2s_band_partition(window_rows, world, rank, ctypes.byref(a), ctypes.byref(b))
+    if rc != S2S_OK:
+        raise S2SError(rc, "bad band partition arguments")
+    return a.value, b.value
+
+
+def band_halo_ops(rank: int, world: int, own_rows: int, rows: int, cyclic: bool):
+    """The transfers of one halo exchange: [(kind, peer, first local row, rows)]."""
+    L = load()
+    buf = (ctypes.c_int * 16)()
+    k = L.s2s_band_halo_ops(rank, world, own_rows, rows, int(cyclic), buf, 16)
+    if k < 0:
+        raise S2SError(S2S_ERR_INVALID, "bad halo arguments")
+    return [tuple(buf[4 * i:4 * i + 4]) for i in range(k)]

@@ -73,7 +73,7 @@ template <int DP, int HPC>
 __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     const __half* __restrict__ qkv, __half* __restrict__ out, const float* __restrict__ cpb,
     const float* __restrict__ lscale, const int* __restrict__ rows, int heads, int hd, int ld_out,
-    int nwh, int nww, int hp, int wp, int shift, int nwin_total) {
+    int nwh, int nww, int hp, int wp, int shift, int nwin_total, int wh_off) {
   constexpr int N = 64;
   constexpr int NS = N + 8;                    // padded bias row (floats)
   constexpr int SEG = HPC * 3 * DP;            // halves of this CTA's heads per token row
@@ -166,7 +166,10 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     const __half* sq = sqb + (size_t)b * N * SSTRIDE;
     const uint32_t sbase = sbase0 + (uint32_t)(b * N * SSTRIDE * 2);
     const int wi = win % nw;
-    const int wh = wi / nww, ww = wi % nww;
+    // window row on the (global) hp x wp plane the shift mask is defined on
+    int wh = wi / nww + wh_off;
+    if (wh < 0) wh += hp / 8;
+    const int ww = wi % nww;
     const size_t tok0 = (size_t)win * N;
 
     // 1/|k| for keys lane and lane+32, 1/|q| for this thread's two query rows.
@@ -292,7 +295,7 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
 template <int DP, int HPC>
 cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb, const float* lscale,
                           const int* rows, int nwin_total, int heads, int hd, int ld_out, int nwh,
-                          int nww, int hp, int wp, int shift, cudaStream_t st) {
+                          int nww, int hp, int wp, int shift, int wh_off, cudaStream_t st) {
   constexpr int SEG = HPC * 3 * DP;
   const size_t smem = (size_t)HPC * 64 * 72 * 4 + (size_t)2 * 64 * (SEG + 8) * 2 + 5 * 8 + 16;
   static int ctas = 0;  // resident CTAs per device
@@ -315,7 +318,7 @@ cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb, cons
   G = (G / NG) * NG;
   if (G < NG) G = NG;
   k_window_attention<DP, HPC><<<(unsigned)G, 128 * HPC + 32, smem, st>>>(
-      qkv, out, cpb, lscale, rows, heads, hd, ld_out, nwh, nww, hp, wp, shift, nwin_total);
+      qkv, out, cpb, lscale, rows, heads, hd, ld_out, nwh, nww, hp, wp, shift, nwin_total, wh_off);
   return cudaGetLastError();
 }
 
@@ -324,20 +327,20 @@ cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb, cons
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
                                     const float* lscale, const int* rows, int nwin_total,
                                     int heads, int hd, int dp, int ld_out, int nwh, int nww,
-                                    int hp, int wp, int shift, cudaStream_t st) {
+                                    int hp, int wp, int shift, int wh_off, cudaStream_t st) {
   const bool pair = heads % 2 == 0;
   if (dp == 32 && pair)
     return launch_attn_t<32, 2>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, st);
+                                nww, hp, wp, shift, wh_off, st);
   if (dp == 32)
     return launch_attn_t<32, 1>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, st);
+                                nww, hp, wp, shift, wh_off, st);
   if (dp == 16 && pair)
     return launch_attn_t<16, 2>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, st);
+                                nww, hp, wp, shift, wh_off, st);
   if (dp == 16)
     return launch_attn_t<16, 1>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, st);
+                                nww, hp, wp, shift, wh_off, st);
   return cudaErrorInvalidValue;
 }
 

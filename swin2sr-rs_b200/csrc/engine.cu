@@ -28,15 +28,18 @@
 
 #include "common.cuh"
 #include "gemm_tc.cuh"
+#include "halo.cuh"
 #include "s2s.h"
 
 namespace s2s {
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
                                     const float* lscale, const int* rows, int nwin_total,
                                     int heads, int hd, int dp, int ld_out, int nwh, int nww,
-                                    int hp, int wp, int shift, cudaStream_t st);
+                                    int hp, int wp, int shift, int wh_off, cudaStream_t st);
 cudaError_t launch_pad_reflect(const float* x, float* y, int B, int c, int h, int w, int hp,
                                int wp, cudaStream_t st);
+cudaError_t launch_pad_band(const float* x, float* y, int c, int h, int w, int hp, int wp, int rows,
+                            int y0, cudaStream_t st);
 cudaError_t launch_conv3_small(const float* in, const float* wgt, const float* bias, int B, int H,
                                int W, int co_n, int act, float slope, float* o32, int ld32,
                                __half* o16, int ld16, cudaStream_t st);
@@ -87,10 +90,27 @@ struct Stage {
   TcWeight conv, pe;
 };
 
-// Activation workspace for one (B, h, w).
+// Activation workspace for one (B, h, w), over a local plane of hp x wp tokens per image.
+//
+// Whole-image plans: the local plane is the padded plane and every row is owned.
+// Band plans (one rank of a sharded forward, B = 1): the local plane holds global
+// padded rows [R0 - 8, R1 + 8); rows [8, 8 + R1 - R0) are owned, the 8 rows on
+// either side receive neighbours' rows before the steps that read them.
 struct Plan {
   int B = 0, h = 0, w = 0, hp = 0, wp = 0;
   size_t T = 0;
+  int band = 0, rank = 0, world = 1, R0 = 0, R1 = 0, ghp = 0;
+  int halo = 0;         // local rows above the owned rows
+  int own_rows = 0;     // owned plane rows
+  size_t own_off = 0;   // tokens before the first owned row
+  int M_own = 0;        // owned tokens (the per-token GEMMs' M)
+  size_t sh_off = 0;    // tokens before the first row the shifted windows cover
+  int M_sh = 0;         // tokens the shifted blocks' QKV covers
+  int nwin[2] = {0, 0}, nwh_l[2] = {0, 0}, wh_off[2] = {0, 0};  // attention, shift 0 / win/2
+  int conv_row0 = 0, conv_H = 0, conv_y0 = 0, conv_y1 = 0;  // 3x3 conv: map rows, output rows
+  int head_row0 = 0, head_rows = 0;  // the plane the upsampling head runs on
+  int crop_y0 = 0, crop_rows = 0;    // output LR rows: head plane rows [crop_y0, +crop_rows)
+  CUtensorMap mX16s;                 // QKV operand of the shifted blocks
   std::vector<void*> allocs;
   size_t bytes = 0;
   float *P = nullptr, *F0 = nullptr, *X = nullptr, *S = nullptr;
@@ -139,6 +159,10 @@ struct s2s_handle {
   bool fused_mlp = false;      // (Cp, HIDp) has a fused MLP kernel
   long long stop_after = -1;   // diagnostics: launches per forward before stopping
   long long fwd_launches = 0;  // launches enqueued by the forward in flight
+  // Row-band sharding (s2s_band_init / s2s_band_init_local): this handle's rank.
+  int band_rank = 0, band_world = 1;
+  void* nccl_comm = nullptr;                  // ncclComm_t
+  std::shared_ptr<s2s::LocalGroup> group;     // in-process group instead of NCCL
 };
 
 namespace {
@@ -400,7 +424,7 @@ int64_t plan_bytes(const s2s_handle* H, int B, int h, int w) {
   b += (int64_t)B * 3 * hp * wp * 4;        // P
   b += 3 * T * Cp * 4;                      // F0, X, S
   b += 3 * T * Cp * 2;                      // F0h, X16, AO
-  b += T * H->NQ * 2 + T * H->HIDp * 2;     // QKV, H16
+  b += T * H->NQ * 2 + (H->fused_mlp ? 0 : T * H->HIDp * 2);  // QKV, H16 (unfused MLP)
   b += 2 * T * 4;                           // window row tables
   b += T * 64 * 2 + 3 * T * s * s * 64 * 2; // head planes
   if (H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX)
@@ -409,7 +433,9 @@ int64_t plan_bytes(const s2s_handle* H, int B, int h, int w) {
 }
 
 Plan* get_plan(s2s_handle* H, int B, int h, int w) {
-  if (H->plan && H->plan->B == B && H->plan->h == h && H->plan->w == w) return H->plan.get();
+  const int band = H->band_world > 1;
+  if (H->plan && H->plan->B == B && H->plan->h == h && H->plan->w == w && H->plan->band == band)
+    return H->plan.get();
   if (H->plan) {
     ck(cudaStreamSynchronize(H->stream), "plan change");
     free_plan(*H->plan);
@@ -420,12 +446,65 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
   P->B = B;
   P->h = h;
   P->w = w;
-  P->hp = (h / win + 1) * win;
+  P->ghp = (h / win + 1) * win;
   P->wp = (w / win + 1) * win;
-  const int hp = P->hp, wp = P->wp;
+  const int wp = P->wp, nww = wp / 8;
+  if (!band) {
+    P->hp = P->ghp;
+    P->own_rows = P->hp;
+    P->M_own = P->M_sh = B * P->hp * wp;
+    for (int i = 0; i < 2; i++) {
+      P->nwh_l[i] = P->hp / 8;
+      P->nwin[i] = B * P->nwh_l[i] * nww;
+    }
+    P->conv_H = P->conv_y1 = P->hp;
+    P->head_rows = P->hp;
+    P->crop_rows = h;
+  } else {
+    if (B != 1) fail(S2S_ERR_INVALID, "a row-band sharded forward takes one image");
+    P->band = 1;
+    P->rank = H->band_rank;
+    P->world = H->band_world;
+    int w0, w1;
+    if (P->world > P->ghp / 8)
+      fail(S2S_ERR_INVALID, std::to_string(P->world) + " bands need at least as many window "
+                            "rows; the padded plane has " + std::to_string(P->ghp / 8));
+    band_partition(P->ghp / 8, P->world, P->rank, &w0, &w1);
+    P->R0 = 8 * w0;
+    P->R1 = 8 * w1;
+    const int nb = w1 - w0;
+    P->halo = 8;
+    P->own_rows = 8 * nb;
+    P->hp = P->own_rows + 2 * P->halo;
+    P->own_off = (size_t)P->halo * wp;
+    P->M_own = P->own_rows * wp;
+    // shifted windows cover global rows [R0 - 4, R1 + 4): local [4, hp - 4)
+    P->sh_off = (size_t)(P->halo - 4) * wp;
+    P->M_sh = (P->own_rows + 8) * wp;
+    P->nwh_l[0] = nb;
+    P->nwin[0] = nb * nww;
+    P->wh_off[0] = w0;
+    P->nwh_l[1] = nb + 1;
+    P->nwin[1] = (nb + 1) * nww;
+    P->wh_off[1] = w0 - 1;
+    // 3x3 convs: the map starts one row above the owned rows and ends one below
+    P->conv_row0 = P->halo - 1;
+    P->conv_H = P->own_rows + 2;
+    P->conv_y0 = 1;
+    P->conv_y1 = P->own_rows + 1;
+    // the head: 4 neighbour rows on interior sides (its receptive field is under 3
+    // low-resolution rows), the plane's own edge on the outer ones
+    P->head_row0 = P->rank == 0 ? P->halo : P->halo - 4;
+    const int head_end = P->halo + P->own_rows + (P->rank == P->world - 1 ? 0 : 4);
+    P->head_rows = head_end - P->head_row0;
+    P->crop_y0 = P->halo - P->head_row0;
+    P->crop_rows = std::max(0, std::min(P->R1, h) - P->R0);
+  }
+  const int hp = P->hp;
   const size_t T = (size_t)B * hp * wp;
   P->T = T;
   const int Cp = H->Cp, s = H->cfg.scale;
+  const size_t Th = (size_t)B * P->head_rows * wp;  // head plane tokens
   try {
     P->P = (float*)dalloc(*P, (size_t)B * 3 * hp * wp * 4);
     P->F0 = (float*)dalloc(*P, T * Cp * 4);
@@ -435,10 +514,10 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
     P->X16 = (__half*)dalloc(*P, T * Cp * 2);
     P->AO = (__half*)dalloc(*P, T * Cp * 2);
     P->QKV = (__half*)dalloc(*P, T * H->NQ * 2);
-    P->H16 = (__half*)dalloc(*P, T * H->HIDp * 2);
-    for (int i = 0; i < 2; i++) P->rows[i] = (int*)dalloc(*P, T * 4);
-    P->HA = (__half*)dalloc(*P, T * 64 * 2);
-    for (int i = 0; i < 3; i++) P->HB[i] = (__half*)dalloc(*P, T * s * s * 64 * 2);
+    if (!H->fused_mlp) P->H16 = (__half*)dalloc(*P, T * H->HIDp * 2);
+    for (int i = 0; i < 2; i++) P->rows[i] = (int*)dalloc(*P, (size_t)P->nwin[i] * 64 * 4);
+    P->HA = (__half*)dalloc(*P, Th * 64 * 2);
+    for (int i = 0; i < 3; i++) P->HB[i] = (__half*)dalloc(*P, Th * s * s * 64 * 2);
     if (H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX) {
       P->BIC = (float*)dalloc(*P, (size_t)B * 3 * hp * s * wp * s * 4);
       P->BICF = (float*)dalloc(*P, T * s * s * 64 * 4);
@@ -448,37 +527,52 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
     free_plan(*P);
     throw;
   }
-  // Window row tables (batch-offset): window-major token r of each image -> image row.
+  // Window row tables: window-major token -> local plane row.
   {
-    const int hw = hp * wp;
     std::vector<int> rt[2];
-    for (auto& v : rt) v.resize(T);
-    for (int b = 0; b < B; b++) {
-      const int o = b * hw;
-      for (int r = 0; r < hw; r++) {
-        rt[0][o + r] = o + token_pixel(r, hp, wp, 0);
-        rt[1][o + r] = o + token_pixel(r, hp, wp, win / 2);
+    if (!band) {
+      const int hw = hp * wp;
+      for (auto& v : rt) v.resize(T);
+      for (int b = 0; b < B; b++) {
+        const int o = b * hw;
+        for (int r = 0; r < hw; r++) {
+          rt[0][o + r] = o + token_pixel(r, hp, wp, 0);
+          rt[1][o + r] = o + token_pixel(r, hp, wp, win / 2);
+        }
+      }
+    } else {
+      // unshifted: the owned window rows; shifted: window rows straddling them,
+      // local rows [4 + 8j, 12 + 8j), columns rolled by 4 with the plane's wrap
+      for (int sh = 0; sh < 2; sh++) {
+        rt[sh].resize((size_t)P->nwin[sh] * 64);
+        const int y00 = sh ? P->halo - 4 : P->halo, x0 = sh ? win / 2 : 0;
+        for (int wi = 0; wi < P->nwin[sh]; wi++)
+          for (int t = 0; t < 64; t++) {
+            const int y = y00 + (wi / nww) * 8 + t / 8;
+            const int x = ((wi % nww) * 8 + t % 8 + x0) % wp;
+            rt[sh][(size_t)wi * 64 + t] = y * wp + x;
+          }
       }
     }
     for (int i = 0; i < 2; i++)
-      ck(cudaMemcpy(P->rows[i], rt[i].data(), T * 4, cudaMemcpyHostToDevice), "row table upload");
+      ck(cudaMemcpy(P->rows[i], rt[i].data(), rt[i].size() * 4, cudaMemcpyHostToDevice),
+         "row table upload");
   }
-  // TMA maps over the activation buffers.
+  // TMA maps over the activation buffers (the per-token GEMMs read the owned rows).
   bool ok = true;
-  ok &= make_map_rows(&P->mF0h, P->F0h, T, Cp, 128);
-  {
-    ok &= make_map_rows(&P->mX16, P->X16, T, Cp, 128);
-    int bw, bh;
-    conv_box(wp, &bw, &bh);
-    ok &= make_map_nhwc(&P->cX16, P->X16, B, hp, wp, Cp, bw, bh);
-  }
-  ok &= make_map_rows(&P->mAO, P->AO, T, Cp, 128);
-  ok &= make_map_rows(&P->mH16, P->H16, T, H->HIDp, 128);
+  ok &= make_map_rows(&P->mF0h, P->F0h + P->own_off * Cp, P->M_own, Cp, 128);
+  ok &= make_map_rows(&P->mX16, P->X16 + P->own_off * Cp, P->M_own, Cp, 128);
+  ok &= make_map_rows(&P->mX16s, P->X16 + P->sh_off * Cp, P->M_sh, Cp, 128);
+  ok &= make_map_rows(&P->mAO, P->AO + P->own_off * Cp, P->M_own, Cp, 128);
+  if (P->H16) ok &= make_map_rows(&P->mH16, P->H16 + P->own_off * H->HIDp, P->M_own, H->HIDp, 128);
   {
     int bw, bh;
     conv_box(wp, &bw, &bh);
-    ok &= make_map_nhwc(&P->cAO, P->AO, B, hp, wp, Cp, bw, bh);
-    ok &= make_map_nhwc(&P->cHA, P->HA, B, hp, wp, 64, bw, bh);
+    ok &= make_map_nhwc(&P->cX16, P->X16 + (size_t)P->conv_row0 * wp * Cp, B, P->conv_H, wp, Cp,
+                        bw, bh);
+    ok &= make_map_nhwc(&P->cAO, P->AO + (size_t)P->head_row0 * wp * Cp, B, P->head_rows, wp, Cp,
+                        bw, bh);
+    ok &= make_map_nhwc(&P->cHA, P->HA, B, P->head_rows, wp, 64, bw, bh);
   }
   for (int i = 0; i < 3; i++)
     for (int r = 0; r < 3; r++) {
@@ -486,7 +580,7 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
       if (f > s && r > 0) continue;
       int bw, bh;
       conv_box(wp * f, &bw, &bh);
-      ok &= make_map_nhwc(&P->cHB[i][r], P->HB[i], B, hp * f, wp * f, 64, bw, bh);
+      ok &= make_map_nhwc(&P->cHB[i][r], P->HB[i], B, P->head_rows * f, wp * f, 64, bw, bh);
     }
   if (!ok) {
     free_plan(*P);
@@ -529,6 +623,25 @@ struct Launcher {
       H->prof_pending.push_back({name, a, b});
     }
   }
+  // A transfer between bands (NCCL's kernels or copies, not ours): timed like a
+  // launch, not counted as one.
+  template <typename F>
+  void comm(const char* name, F&& f) {
+    if (H->stop_after >= 0 && H->fwd_launches >= H->stop_after) return;
+    const bool timed = H->profiling && (H->prof_only.empty() ||
+                                        strncmp(name, H->prof_only.c_str(), H->prof_only.size()) == 0);
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (timed) {
+      a = ev();
+      b = ev();
+      ck(cudaEventRecord(a, st), "event");
+    }
+    f();
+    if (timed) {
+      ck(cudaEventRecord(b, st), "event");
+      H->prof_pending.push_back({name, a, b});
+    }
+  }
 };
 
 Epi epi0() {
@@ -550,7 +663,8 @@ GemmArgs gemm_args(int M, int N, int K, const Epi& e) {
   return a;
 }
 
-GemmArgs conv_args(int B, int H, int W, int Cip, int N, const Epi& e) {
+// A 3x3 convolution over the B x H x W plane of the A map, writing output rows [y0, y1).
+GemmArgs conv_args(int B, int H, int W, int Cip, int N, const Epi& e, int y0, int y1) {
   GemmArgs a;
   memset(&a, 0, sizeof a);
   a.conv = 1;
@@ -562,7 +676,9 @@ GemmArgs conv_args(int B, int H, int W, int Cip, int N, const Epi& e) {
   a.kc = Cip / 64;
   conv_box(W, &a.boxw, &a.boxh);
   a.tiles_x = (W + a.boxw - 1) / a.boxw;
-  a.tiles_y = (H + a.boxh - 1) / a.boxh;
+  a.y_off = y0;
+  a.y_end = y1;
+  a.tiles_y = (y1 - y0 + a.boxh - 1) / a.boxh;
   a.epi = e;
   a.epi.n_valid = e.n_valid ? e.n_valid : N;
   return a;
@@ -601,6 +717,73 @@ void set_final(const s2s_handle* H, Epi& e) {
   e.mean2 = H->cfg.mean[2];
 }
 
+// ------------------------------------------------------------------ band halos
+// Exchange `n` plane rows of `buf` ([local plane][ld] fp16) with the neighbouring
+// bands (halo_ops); without `cyclic`, halo rows beyond the plane's true edges are
+// zeroed when `zero_edges`.
+void halo_exchange(s2s_handle* H, Plan* P, __half* buf, int ld, int n, bool cyclic,
+                   bool zero_edges, cudaStream_t st) {
+  const size_t row = (size_t)P->wp * ld;  // halves per plane row
+  HaloOp ops[4];
+  const int k = halo_ops(P->rank, P->world, P->halo, P->own_rows, n, cyclic, ops);
+  if (H->nccl_comm) {
+    const NcclApi& api = nccl_api();
+    ncclComm_t comm = (ncclComm_t)H->nccl_comm;
+    auto nck = [&](ncclResult_t r) {
+      if (r != ncclSuccess)
+        fail(S2S_ERR_NCCL, std::string("halo exchange: ") + api.GetErrorString(r));
+    };
+    nck(api.GroupStart());
+    for (int i = 0; i < k; i++) {
+      __half* p = buf + (size_t)ops[i].row0 * row;
+      if (ops[i].kind == 0)
+        nck(api.Send(p, (size_t)ops[i].rows * row, ncclFloat16, ops[i].peer, comm, st));
+      else
+        nck(api.Recv(p, (size_t)ops[i].rows * row, ncclFloat16, ops[i].peer, comm, st));
+    }
+    nck(api.GroupEnd());
+  } else if (H->group) {
+    LocalGroup& G = *H->group;
+    const int r = P->rank;
+    G.buf[r] = reinterpret_cast<const char*>(buf);
+    G.halo[r] = P->halo;
+    G.own_rows[r] = P->own_rows;
+    ck(cudaEventRecord(G.ready[r], st), "halo event");
+    if (!G.barrier(120.0)) fail(S2S_ERR_TIMEOUT, "halo exchange: a band of the group never arrived");
+    const size_t rb = row * 2;
+    for (int i = 0; i < k; i++) {
+      if (ops[i].kind != 1) continue;
+      const int q = ops[i].peer;
+      // from the rank above: its last n owned rows; from below: its first n
+      const bool from_above = ops[i].row0 < P->halo;
+      const int src_row = from_above ? G.halo[q] + G.own_rows[q] - n : G.halo[q];
+      ck(cudaStreamWaitEvent(st, G.ready[q], 0), "halo wait");
+      ck(cudaMemcpyAsync(buf + (size_t)ops[i].row0 * row, G.buf[q] + (size_t)src_row * rb,
+                         (size_t)n * rb, cudaMemcpyDeviceToDevice, st),
+         "halo copy");
+    }
+    ck(cudaEventRecord(G.done[r], st), "halo event");
+    if (!G.barrier(120.0)) fail(S2S_ERR_TIMEOUT, "halo exchange: a band of the group never arrived");
+    // my rows are read by both neighbours' copies: later writes wait for them
+    const int prev = (r + P->world - 1) % P->world, next = (r + 1) % P->world;
+    ck(cudaStreamWaitEvent(st, G.done[prev], 0), "halo wait");
+    ck(cudaStreamWaitEvent(st, G.done[next], 0), "halo wait");
+  } else {
+    fail(S2S_ERR_INVALID, "band forward without a communicator");
+  }
+  if (!cyclic && zero_edges) {
+    if (P->rank == 0)
+      ck(cudaMemsetAsync(buf + (size_t)(P->halo - n) * row, 0, n * row * 2, st), "halo zero");
+    if (P->rank == P->world - 1)
+      ck(cudaMemsetAsync(buf + (size_t)(P->halo + P->own_rows) * row, 0, n * row * 2, st),
+         "halo zero");
+  }
+}
+
+// ------------------------------------------------------------------ the forward
+// One forward over the plan's plane: the whole padded image (B images), or, for a
+// sharded forward, this rank's row band (the owned rows' output only; d_out is then
+// [3][crop_rows * s][w * s]).
 void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float* d_out,
                     float* d_aux, cudaStream_t st) {
   const s2s_config& c = H->cfg;
@@ -613,14 +796,27 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
   H->fwd_launches = 0;
   Launcher L{H, st};
   const int C = c.embed, Cp = H->Cp, hp = P->hp, wp = P->wp, s = c.scale, F = H->feat;
-  const int M = (int)P->T;
+  const int M = P->M_own;
+  const bool band = P->band != 0;
+  float* const X = P->X + P->own_off * Cp;       // owned rows of the residual stream
+  __half* const X16 = P->X16 + P->own_off * Cp;
+  float* const S = P->S + P->own_off * Cp;
+  auto exchange = [&](const char* name, __half* buf, int n, bool cyclic, bool zero_edges) {
+    L.comm(name, [&] { halo_exchange(H, P, buf, Cp, n, cyclic, zero_edges, st); });
+  };
   // 1. pad + conv_first (fp32 body skip F0, fp16 operand F0h).
-  L.run("pad_reflect", [&] { return launch_pad_reflect(d_in, P->P, B, 3, h, w, hp, wp, st); });
+  if (!band) {
+    L.run("pad_reflect", [&] { return launch_pad_reflect(d_in, P->P, B, 3, h, w, hp, wp, st); });
+  } else {
+    L.run("pad_reflect", [&] {
+      return launch_pad_band(d_in, P->P, 3, h, w, P->ghp, wp, hp, P->R0 - P->halo, st);
+    });
+  }
   L.run("conv_first", [&] {
     return launch_conv3_small(P->P, H->cf_w, H->cf_b, B, hp, wp, C, 0, 0.0f, P->F0, Cp, P->F0h,
                               Cp, st);
   });
-  // 2. top patch_embed: 1x1 + LayerNorm -> X (window order, shift 0), S (image order).
+  // 2. top patch_embed: 1x1 + LayerNorm -> X, X16 and the stage input S.
   {
     Epi e = epi0();
     e.bias = H->pe.b;
@@ -628,33 +824,37 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.ln_b = H->pe_b;
     e.ln_n = C;
     e.n_valid = C;
-    e.o32 = P->X;
+    e.o32 = X;
     e.ld32 = Cp;
-    e.o16 = P->X16;
+    e.o16 = X16;
     e.ld16 = Cp;
-    e.o32b = P->S;
+    e.o32b = S;
     e.ld32b = Cp;
     GemmArgs a = gemm_args(M, Cp, Cp, e);
     L.run("gemm_patch_embed", [&] { return launch_gemm(P->mF0h, H->pe.map, out_maps(P, a), a, Cp, st); });
   }
-  const int nwin = B * (hp / 8) * (wp / 8);
   for (int si = 0; si < c.n_depths; si++) {
     Stage& stg = H->stages[si];
     const int depth = c.depths[si];
     for (int b = 0; b < depth; b++) {
       Block& bl = stg.blocks[b];
       const int sh = (b % 2 == 1) ? c.window / 2 : 0;
+      const int k = sh ? 1 : 0;
+      // the shifted windows reach 4 rows into each neighbouring band (cyclically)
+      if (band && sh) exchange("halo_shift", P->X16, 4, true, false);
       {  // QKV
         Epi e = epi0();
         e.bias = bl.qkv.b;
-        e.o16 = P->QKV;
+        e.o16 = P->QKV + (sh ? P->sh_off : P->own_off) * H->NQ;
         e.ld16 = H->NQ;
-        GemmArgs a = gemm_args(M, H->NQ, Cp, e);
-        L.run("gemm_qkv", [&] { return launch_gemm(P->mX16, bl.qkv.map, out_maps(P, a), a, bl.qkv.BN, st); });
+        GemmArgs a = gemm_args(sh ? P->M_sh : M, H->NQ, Cp, e);
+        const CUtensorMap& mA = sh ? P->mX16s : P->mX16;
+        L.run("gemm_qkv", [&] { return launch_gemm(mA, bl.qkv.map, out_maps(P, a), a, bl.qkv.BN, st); });
       }
       L.run("window_attention", [&] {
-        return launch_window_attention(P->QKV, P->AO, bl.cpb, bl.ls, P->rows[sh ? 1 : 0], nwin,
-                                       H->heads, H->hd, H->DP, Cp, hp / 8, wp / 8, hp, wp, sh, st);
+        return launch_window_attention(P->QKV, P->AO, bl.cpb, bl.ls, P->rows[k], P->nwin[k],
+                                       H->heads, H->hd, H->DP, Cp, P->nwh_l[k], wp / 8, P->ghp,
+                                       wp, sh, P->wh_off[k], st);
       });
       {  // proj + norm1 + residual, in place
         Epi e = epi0();
@@ -663,11 +863,11 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.ln_b = bl.n1b;
         e.ln_n = C;
         e.n_valid = C;
-        e.res_post = P->X;
+        e.res_post = X;
         e.ld_res_post = Cp;
-        e.o32 = P->X;
+        e.o32 = X;
         e.ld32 = Cp;
-        e.o16 = P->X16;
+        e.o16 = X16;
         e.ld16 = Cp;
         GemmArgs a = gemm_args(M, Cp, Cp, e);
         L.run("gemm_proj", [&] { return launch_gemm(P->mAO, bl.proj.map, out_maps(P, a), a, Cp, st); });
@@ -681,13 +881,13 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         m.beta2 = bl.n2b;
         m.ln_n = C;
         m.ln_eps = 1e-5f;
-        m.x = P->X;
-        m.x16 = P->X16;
+        m.x = X;
+        m.x16 = X16;
         L.run("mlp_fused", [&] {
           Epi eo = epi0();
-          eo.o32 = P->X;
+          eo.o32 = X;
           eo.ld32 = Cp;
-          eo.o16 = P->X16;
+          eo.o16 = X16;
           eo.ld16 = Cp;
           const OutMaps om = out_maps(P, gemm_args(M, Cp, Cp, eo));
           return launch_mlp(P->mX16, bl.fc1.map, bl.fc2.map, om.o32, om.o16, m, Cp, H->HIDp, st);
@@ -697,7 +897,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
           Epi e = epi0();
           e.bias = bl.fc1.b;
           e.act = ACT_GELU;
-          e.o16 = P->H16;
+          e.o16 = P->H16 + P->own_off * H->HIDp;
           e.ld16 = H->HIDp;
           GemmArgs a = gemm_args(M, H->HIDp, Cp, e);
           L.run("gemm_fc1", [&] { return launch_gemm(P->mX16, bl.fc1.map, out_maps(P, a), a, bl.fc1.BN, st); });
@@ -709,11 +909,11 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
           e.ln_b = bl.n2b;
           e.ln_n = C;
           e.n_valid = C;
-          e.res_post = P->X;
+          e.res_post = X;
           e.ld_res_post = Cp;
-          e.o32 = P->X;
+          e.o32 = X;
           e.ld32 = Cp;
-          e.o16 = P->X16;
+          e.o16 = X16;
           e.ld16 = Cp;
           GemmArgs a = gemm_args(M, Cp, H->HIDp, e);
           L.run("gemm_fc2", [&] { return launch_gemm(P->mH16, bl.fc2.map, out_maps(P, a), a, Cp, st); });
@@ -721,13 +921,14 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       }
     }
     // RSTB tail: conv3x3 -> 1x1 patch_embed + stage residual.
+    if (band) exchange("halo_conv", P->X16, 1, false, true);
     {
       Epi e = epi0();
       e.bias = stg.conv.b;
       e.n_valid = C;
-      e.o16 = P->AO;
+      e.o16 = P->AO + (size_t)P->conv_row0 * wp * Cp;
       e.ld16 = Cp;
-      GemmArgs a = conv_args(B, hp, wp, Cp, Cp, e);
+      GemmArgs a = conv_args(B, P->conv_H, wp, Cp, Cp, e, P->conv_y0, P->conv_y1);
       L.run("conv_stage", [&] { return launch_gemm(P->cX16, stg.conv.map, out_maps(P, a), a, Cp, st); });
     }
     {
@@ -738,24 +939,24 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       // the stage residual: without a norm it is added after the bias (TMA path); the
       // last stage's final LayerNorm normalises the sum, so there it comes first
       if (last) {
-        e.res_pre = P->S;
+        e.res_pre = S;
         e.ld_res_pre = Cp;
       } else {
-        e.res_post = P->S;
+        e.res_post = S;
         e.ld_res_post = Cp;
       }
       if (!last) {
-        e.o32 = P->X;
+        e.o32 = X;
         e.ld32 = Cp;
-        e.o16 = P->X16;
+        e.o16 = X16;
         e.ld16 = Cp;
-        e.o32b = P->S;
+        e.o32b = S;
         e.ld32b = Cp;
       } else {  // + final norm, image order, fp16 operand of conv_after_body
         e.ln_g = H->nrm_g;
         e.ln_b = H->nrm_b;
         e.ln_n = C;
-        e.o16 = P->X16;
+        e.o16 = X16;
         e.ld16 = Cp;
       }
       GemmArgs a = gemm_args(M, Cp, Cp, e);
@@ -764,21 +965,24 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     }
   }
   // 3. conv_after_body + body skip (conv_first output) -> Y16 (in AO).
+  if (band) exchange("halo_conv", P->X16, 1, false, true);
   {
     Epi e = epi0();
     e.bias = H->cab.b;
     e.n_valid = C;
-    e.res_post = P->F0;
+    e.res_post = P->F0 + (size_t)P->conv_row0 * wp * Cp;
     e.ld_res_post = Cp;
-    e.o16 = P->AO;
+    e.o16 = P->AO + (size_t)P->conv_row0 * wp * Cp;
     e.ld16 = Cp;
-    GemmArgs a = conv_args(B, hp, wp, Cp, Cp, e);
+    GemmArgs a = conv_args(B, P->conv_H, wp, Cp, Cp, e, P->conv_y0, P->conv_y1);
     L.run("conv_after_body", [&] { return launch_gemm(P->cX16, H->cab.map, out_maps(P, a), a, Cp, st); });
   }
-  // 4. head.
+  // 4. head, on its own plane: head_rows x wp (the whole padded plane unless banded).
+  if (band) exchange("halo_head", P->AO, 4, false, false);
+  const int hh0 = P->head_rows;
   auto conv_to = [&](const char* name, const CUtensorMap& mapA, const TcWeight& tw, int Hh, int Ww,
                      int Cip, Epi e) {
-    GemmArgs a = conv_args(B, Hh, Ww, Cip, tw.N, e);
+    GemmArgs a = conv_args(B, Hh, Ww, Cip, tw.N, e, 0, Hh);
     L.run(name, [&] { return launch_gemm(mapA, tw.map, out_maps(P, a), a, tw.BN, st); });
   };
   auto cbu = [&]() {
@@ -788,14 +992,15 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.slope = 0.01f;
     e.o16 = P->HA;
     e.ld16 = F;
-    conv_to("conv_before_upsample", P->cAO, H->cbu, hp, wp, Cp, e);
+    conv_to("conv_before_upsample", P->cAO, H->cbu, hh0, wp, Cp, e);
   };
   auto final_planes = [&](const CUtensorMap& mapA, int Hh, int Ww) {
     Epi e = epi0();
     e.bias = H->last.b;
     e.store = STORE_PLANES;
     e.planes = d_out;
-    e.crop_h = h * s;
+    e.crop_y0 = P->crop_y0 * s;
+    e.crop_h = P->crop_rows * s;
     e.crop_w = w * s;
     set_final(H, e);
     conv_to("conv_last", mapA, H->last, Hh, Ww, F, e);
@@ -805,9 +1010,10 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     case S2S_PIXELSHUFFLE_AUX: {
       cbu();
       const CUtensorMap* src = &P->cHA;
-      int hh = hp, ww = wp;
+      int hh = hh0, ww = wp;
       const int octs = (int)std::lround(std::log2((double)s));
       if (c.upsampler == S2S_PIXELSHUFFLE_AUX) {
+        if (band) fail(S2S_ERR_UNSUPPORTED, "the pixelshuffle_aux head has no band mode");
         // bicubic branch of the padded, mean-adjusted input, on the padded output grid
         L.run("bicubic", [&] {
           return launch_bicubic(P->P, P->BIC, B * 3, hp, wp, hp * s, wp * s, st);
@@ -852,15 +1058,16 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       e.store = STORE_DIRECT;
       e.planes = d_out;
       e.scale = s;
-      e.crop_h = h * s;
+      e.crop_y0 = P->crop_y0 * s;
+      e.crop_h = P->crop_rows * s;
       e.crop_w = w * s;
       set_final(H, e);
-      conv_to("conv_upsample_direct", P->cAO, H->direct, hp, wp, Cp, e);
+      conv_to("conv_upsample_direct", P->cAO, H->direct, hh0, wp, Cp, e);
       break;
     }
     case S2S_NEARESTCONV: {
       cbu();
-      L.run("upsample_nearest", [&] { return launch_up2_nhwc(P->HA, P->HB[0], B, hp, wp, F, st); });
+      L.run("upsample_nearest", [&] { return launch_up2_nhwc(P->HA, P->HB[0], B, hh0, wp, F, st); });
       {
         Epi e = epi0();
         e.bias = H->up1.b;
@@ -868,10 +1075,10 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.slope = 0.2f;
         e.o16 = P->HB[1];
         e.ld16 = F;
-        conv_to("conv_up1", P->cHB[0][1], H->up1, 2 * hp, 2 * wp, F, e);
+        conv_to("conv_up1", P->cHB[0][1], H->up1, 2 * hh0, 2 * wp, F, e);
       }
       L.run("upsample_nearest",
-            [&] { return launch_up2_nhwc(P->HB[1], P->HB[0], B, 2 * hp, 2 * wp, F, st); });
+            [&] { return launch_up2_nhwc(P->HB[1], P->HB[0], B, 2 * hh0, 2 * wp, F, st); });
       {
         Epi e = epi0();
         e.bias = H->up2.b;
@@ -879,7 +1086,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.slope = 0.2f;
         e.o16 = P->HB[2];
         e.ld16 = F;
-        conv_to("conv_up2", P->cHB[0][2], H->up2, 4 * hp, 4 * wp, F, e);
+        conv_to("conv_up2", P->cHB[0][2], H->up2, 4 * hh0, 4 * wp, F, e);
       }
       {
         Epi e = epi0();
@@ -888,9 +1095,9 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.slope = 0.2f;
         e.o16 = P->HB[0];
         e.ld16 = F;
-        conv_to("conv_hr", P->cHB[2][2], H->hr, 4 * hp, 4 * wp, F, e);
+        conv_to("conv_hr", P->cHB[2][2], H->hr, 4 * hh0, 4 * wp, F, e);
       }
-      final_planes(P->cHB[0][2], 4 * hp, 4 * wp);
+      final_planes(P->cHB[0][2], 4 * hh0, 4 * wp);
       break;
     }
     default:
@@ -945,6 +1152,35 @@ void ensure_staging(s2s_handle* H, float** p, size_t* have, size_t n) {
   *have = 0;
   ck(cudaMalloc((void**)p, n * 4), "staging");
   *have = n;
+}
+
+const char* const kBandHandle =
+    "this handle is one band of a sharded forward (s2s_band_init): use s2s_forward_band";
+
+// Leave band mode: destroy the communicator / leave the group (the plan is rebuilt
+// for the new geometry on the next forward).
+void release_band(s2s_handle* H) {
+  if (H->nccl_comm) {
+    const NcclApi& api = nccl_api();
+    if (api.ok) api.CommDestroy((ncclComm_t)H->nccl_comm);
+    H->nccl_comm = nullptr;
+  }
+  H->group.reset();
+  H->band_rank = 0;
+  H->band_world = 1;
+}
+
+// Output rows [r0, r1) of an h-row image that `rank` of `world` bands produces.
+void band_out_rows(int h, int window, int world, int rank, int* r0, int* r1) {
+  if (world <= 1) {
+    *r0 = 0;
+    *r1 = h;
+    return;
+  }
+  int w0, w1;
+  band_partition((h / window + 1), world, rank, &w0, &w1);
+  *r0 = std::min(8 * w0, h);
+  *r1 = std::min(8 * w1, h);
 }
 
 }  // namespace
@@ -1013,6 +1249,7 @@ int s2s_forward_device(s2s_handle* H, int batch, int height, int width, const fl
   if (!H) return S2S_ERR_INVALID;
   cudaStream_t st = stream ? (cudaStream_t)stream : H->stream;
   return guarded(H, [&] {
+    if (H->band_world > 1) fail(S2S_ERR_INVALID, kBandHandle);
     if (H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX && !d_aux)
       fail(S2S_ERR_INVALID, "the pixelshuffle_aux head needs an aux buffer on the device path");
     forward_device(H, batch, height, width, d_in, d_out, d_aux, st);
@@ -1023,6 +1260,7 @@ int s2s_forward_batch(s2s_handle* H, int batch, int height, int width, const flo
                       float* aux) {
   if (!H || !in || !out) return S2S_ERR_INVALID;
   return guarded(H, [&] {
+    if (H->band_world > 1) fail(S2S_ERR_INVALID, kBandHandle);
     const int win = H->cfg.window, s = H->cfg.scale;
     const size_t nin = (size_t)batch * 3 * height * width;
     const size_t nout = (size_t)batch * 3 * height * s * width * s;
@@ -1141,10 +1379,150 @@ int64_t s2s_debug_read(s2s_handle* H, const char* name, float* host, int64_t cap
   return (int64_t)n;
 }
 
+int s2s_band_unique_id(void* out, int cap) {
+  const NcclApi& api = nccl_api();
+  if (!api.ok) {
+    g_create_error = api.err;
+    return S2S_ERR_NCCL;
+  }
+  if (!out || cap < (int)sizeof(ncclUniqueId)) {
+    g_create_error = "s2s_band_unique_id: the buffer must hold S2S_BAND_ID_BYTES";
+    return S2S_ERR_INVALID;
+  }
+  ncclUniqueId id;
+  const ncclResult_t r = api.GetUniqueId(&id);
+  if (r != ncclSuccess) {
+    g_create_error = std::string("ncclGetUniqueId: ") + api.GetErrorString(r);
+    return S2S_ERR_NCCL;
+  }
+  memcpy(out, &id, sizeof id);
+  return S2S_OK;
+}
+
+int s2s_band_init(s2s_handle* H, int rank, int world, const void* id, int id_bytes) {
+  if (!H) return S2S_ERR_INVALID;
+  return guarded(H, [&] {
+    if (world < 1 || rank < 0 || rank >= world)
+      fail(S2S_ERR_INVALID, "s2s_band_init: rank must be in [0, world)");
+    if (world > 1 && H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX)
+      fail(S2S_ERR_UNSUPPORTED, "the pixelshuffle_aux head has no band mode (its input is a "
+                                "batch of small images: split the batch instead)");
+    ck(cudaStreamSynchronize(H->stream), "band init");
+    release_band(H);
+    if (world > 1) {
+      if (!id || id_bytes != (int)sizeof(ncclUniqueId))
+        fail(S2S_ERR_INVALID, "s2s_band_init: the id must be the S2S_BAND_ID_BYTES of "
+                              "s2s_band_unique_id");
+      const NcclApi& api = nccl_api();
+      if (!api.ok) fail(S2S_ERR_NCCL, api.err);
+      ncclUniqueId uid;
+      memcpy(&uid, id, sizeof uid);
+      ncclComm_t comm = nullptr;
+      const ncclResult_t r = api.CommInitRank(&comm, world, uid, rank);
+      if (r != ncclSuccess) fail(S2S_ERR_NCCL, std::string("ncclCommInitRank: ") + api.GetErrorString(r));
+      H->nccl_comm = comm;
+    }
+    H->band_rank = rank;
+    H->band_world = world;
+  });
+}
+
+int s2s_band_init_local(s2s_handle** hs, int world) {
+  if (!hs || world < 1) return S2S_ERR_INVALID;
+  for (int i = 0; i < world; i++)
+    if (!hs[i]) return S2S_ERR_INVALID;
+  auto G = std::make_shared<LocalGroup>();
+  G->world = world;
+  G->buf.assign(world, nullptr);
+  G->halo.assign(world, 0);
+  G->own_rows.assign(world, 0);
+  G->ready.assign(world, nullptr);
+  G->done.assign(world, nullptr);
+  G->device.assign(world, 0);
+  for (int i = 0; i < world; i++) {
+    s2s_handle* H = hs[i];
+    const int rc = guarded(H, [&] {
+      if (world > 1 && H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX)
+        fail(S2S_ERR_UNSUPPORTED, "the pixelshuffle_aux head has no band mode");
+      ck(cudaStreamSynchronize(H->stream), "band init");
+      G->device[i] = H->device;
+      ck(cudaEventCreateWithFlags(&G->ready[i], cudaEventDisableTiming), "band event");
+      ck(cudaEventCreateWithFlags(&G->done[i], cudaEventDisableTiming), "band event");
+    });
+    if (rc != S2S_OK) return rc;
+  }
+  for (int i = 0; i < world; i++) {
+    release_band(hs[i]);
+    hs[i]->group = G;
+    hs[i]->band_rank = i;
+    hs[i]->band_world = world;
+  }
+  return S2S_OK;
+}
+
+int s2s_band_rows(const s2s_handle* H, int height, int* row0, int* row1) {
+  if (!H || height < 1) return S2S_ERR_INVALID;
+  int r0, r1;
+  band_out_rows(height, H->cfg.window, H->band_world, H->band_rank, &r0, &r1);
+  if (row0) *row0 = r0;
+  if (row1) *row1 = r1;
+  return S2S_OK;
+}
+
+int s2s_band_partition(int window_rows, int world, int rank, int* w0, int* w1) {
+  if (window_rows < 1 || world < 1 || world > window_rows || rank < 0 || rank >= world)
+    return S2S_ERR_INVALID;
+  band_partition(window_rows, world, rank, w0, w1);
+  return S2S_OK;
+}
+
+int s2s_band_halo_ops(int rank, int world, int own_rows, int rows, int cyclic, int* ops, int cap) {
+  if (world < 2 || rank < 0 || rank >= world || own_rows < rows || rows < 1 || rows > 8 || !ops ||
+      cap < 16)
+    return -1;
+  HaloOp o[4];
+  const int k = halo_ops(rank, world, 8, own_rows, rows, cyclic != 0, o);
+  for (int i = 0; i < k; i++) {
+    ops[4 * i] = o[i].kind;
+    ops[4 * i + 1] = o[i].peer;
+    ops[4 * i + 2] = o[i].row0;
+    ops[4 * i + 3] = o[i].rows;
+  }
+  return k;
+}
+
+int s2s_forward_band(s2s_handle* H, int height, int width, const float* d_in, float* d_out,
+                     void* stream) {
+  if (!H || !d_in || !d_out) return S2S_ERR_INVALID;
+  cudaStream_t st = stream ? (cudaStream_t)stream : H->stream;
+  return guarded(H, [&] { forward_device(H, 1, height, width, d_in, d_out, nullptr, st); });
+}
+
+int s2s_forward_band_host(s2s_handle* H, int height, int width, const float* in, float* out) {
+  if (!H || !in || !out) return S2S_ERR_INVALID;
+  return guarded(H, [&] {
+    const int s = H->cfg.scale;
+    int r0, r1;
+    band_out_rows(height, H->cfg.window, H->band_world, H->band_rank, &r0, &r1);
+    const size_t nin = (size_t)3 * height * width;
+    const size_t nout = (size_t)3 * (r1 - r0) * s * width * s;
+    ensure_staging(H, &H->h_in, &H->h_in_n, nin);
+    ensure_staging(H, &H->h_out, &H->h_out_n, std::max(nout, (size_t)1));
+    ck(cudaMemcpyAsync(H->h_in, in, nin * 4, cudaMemcpyHostToDevice, H->stream), "upload");
+    forward_device(H, 1, height, width, H->h_in, H->h_out, nullptr, H->stream);
+    if (nout)
+      ck(cudaMemcpyAsync(out, H->h_out, nout * 4, cudaMemcpyDeviceToHost, H->stream), "download");
+    ck(cudaStreamSynchronize(H->stream), "forward");
+    check_device_error(H);
+    if (H->profiling) drain_profile(H);
+  });
+}
+
 void s2s_destroy(s2s_handle* H) {
   if (!H) return;
   cudaSetDevice(H->device);
   cudaDeviceSynchronize();
+  release_band(H);
   drain_profile(H);
   for (cudaEvent_t e : H->ev_pool) cudaEventDestroy(e);
   if (H->plan) free_plan(*H->plan);

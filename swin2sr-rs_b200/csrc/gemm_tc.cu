@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int per_img = a.tiles_x * a.tiles_y;
       bimg = mt / per_img;
       const int rem = mt - bimg * per_img;
-      y0 = (rem / a.tiles_x) * a.boxh;
+      y0 = a.y_off + (rem / a.tiles_x) * a.boxh;
       x0 = (rem % a.tiles_x) * a.boxw;
     }
   };
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       py = y0 + r / a.boxw;
       px = x0 + (r % a.boxw);
-      valid = (py < a.H) && (px < a.W);
+      valid = (py < a.y_end) && (px < a.W);
       mlog = (bimg * a.H + py) * a.W + px;
     }
     if constexpr (STORE == STORE_SHUFFLE2) {
@@ -455,8 +455,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float mean = ch == 0 ? e.mean0 : ch == 1 ? e.mean1 : e.mean2;
           if (e.planes_raw)
             e.planes_raw[((size_t)(bimg * 3 + ch) * a.H + py) * a.W + px] = x;
-          if (e.planes && py < e.crop_h && px < e.crop_w)
-            e.planes[((size_t)(bimg * 3 + ch) * e.crop_h + py) * e.crop_w + px] =
+          const int oy = py - e.crop_y0;
+          if (e.planes && oy >= 0 && oy < e.crop_h && px < e.crop_w)
+            e.planes[((size_t)(bimg * 3 + ch) * e.crop_h + oy) * e.crop_w + px] =
                 x / e.img_range + mean;
         }
       }
@@ -471,9 +472,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col = c * 32 + j;
           if (!valid || col >= nout) continue;
           const int ch = col / s2, rem = col - ch * s2, dy = rem / s, dx = rem - dy * s;
-          const int Y = py * s + dy, X = px * s + dx;
+          const int Y = py * s + dy - e.crop_y0, X = px * s + dx;
           const float mean = ch == 0 ? e.mean0 : ch == 1 ? e.mean1 : e.mean2;
-          if (Y < e.crop_h && X < e.crop_w)
+          if (Y >= 0 && Y < e.crop_h && X < e.crop_w)
             e.planes[((size_t)(bimg * 3 + ch) * e.crop_h + Y) * e.crop_w + X] =
                 pre(v[j], col) / e.img_range + mean;
         }

@@ -50,6 +50,7 @@ struct Epi {
   float* planes;      // denormalised, cropped to crop_h x crop_w (x scale for DIRECT)
   float* planes_raw;  // raw, uncropped [B][3][H][W]
   int crop_h, crop_w, scale;
+  int crop_y0;  // plane row (x scale for DIRECT) written to output row 0
   float img_range;
   float mean0, mean1, mean2;
 };
@@ -59,6 +60,8 @@ struct GemmArgs {
   int conv;     // 0: A is [M][K]; 1: A is the NHWC plane of a 3x3 convolution
   int H, W, B;  // conv plane (output geometry == input geometry)
   int boxw, boxh, tiles_x, tiles_y;
+  int y_off, y_end;  // conv: output rows [y_off, y_end) of the H-row plane (rows outside
+                     // are read as the 3x3 halo only)
   int kc;  // conv: 64-channel chunks per tap
   Epi epi;
 };

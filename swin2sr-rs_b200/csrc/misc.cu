@@ -22,6 +22,28 @@ __global__ void k_pad_reflect(const float* __restrict__ x, float* __restrict__ y
   }
 }
 
+// One row band of the padded plane: rows [y0, y0 + rows) of the hp x wp mirror of
+// k_pad_reflect, zero outside [0, hp) (the 3x3 convolution's padding at the plane's
+// true edges).
+__global__ void k_pad_band(const float* __restrict__ x, float* __restrict__ y, int c, int h,
+                           int w, int hp, int wp, int rows, int y0) {
+  const size_t n = (size_t)c * rows * wp;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int xx = (int)(i % wp);
+    const int ly = (int)((i / wp) % rows);
+    const int ch = (int)(i / ((size_t)wp * rows));
+    const int yy = y0 + ly;
+    float v = 0.0f;
+    if (yy >= 0 && yy < hp) {
+      const int sy = yy < h ? yy : 2 * h - 1 - min(yy, 2 * h - 1);
+      const int sx = xx < w ? xx : 2 * w - 1 - min(xx, 2 * w - 1);
+      v = x[((size_t)ch * h + sy) * w + sx];
+    }
+    y[i] = v;
+  }
+}
+
 // 3x3 s1 p1 conv with 3 input channels, NCHW fp32 input -> NHWC outputs.
 // Thread = (pixel, output channel), channel fastest, so stores are contiguous.
 // Taps in the oracle's order: bias first, then ky, kx, ci.
@@ -143,6 +165,12 @@ inline unsigned grid_for(size_t n, int block) {
 cudaError_t launch_pad_reflect(const float* x, float* y, int B, int c, int h, int w, int hp,
                                int wp, cudaStream_t st) {
   k_pad_reflect<<<grid_for((size_t)B * c * hp * wp, 256), 256, 0, st>>>(x, y, B, c, h, w, hp, wp);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pad_band(const float* x, float* y, int c, int h, int w, int hp, int wp, int rows,
+                            int y0, cudaStream_t st) {
+  k_pad_band<<<grid_for((size_t)c * rows * wp, 256), 256, 0, st>>>(x, y, c, h, w, hp, wp, rows, y0);
   return cudaGetLastError();
 }
 
