@@ -111,6 +111,13 @@ struct Plan {
   int head_row0 = 0, head_rows = 0;  // the plane the upsampling head runs on
   int crop_y0 = 0, crop_rows = 0;    // output LR rows: head plane rows [crop_y0, +crop_rows)
   CUtensorMap mX16s;                 // QKV operand of the shifted blocks
+  CUtensorMap mX16t, mX16b;          // band: the 4 halo rows above / below the owned rows
+  // The forward captured as a CUDA graph for one set of I/O pointers: made on the
+  // second forward with the same pointers, replayed from the third on.
+  cudaGraphExec_t gexec = nullptr;
+  const void *g_in = nullptr, *g_out = nullptr, *g_aux = nullptr;
+  int g_seen = 0;
+  long long g_launches = 0;
   std::vector<void*> allocs;
   size_t bytes = 0;
   float *P = nullptr, *F0 = nullptr, *X = nullptr, *S = nullptr;
@@ -157,11 +164,14 @@ struct s2s_handle {
   std::map<std::string, std::pair<long, double>> prof;
   long long launches = 0;
   bool fused_mlp = false;      // (Cp, HIDp) has a fused MLP kernel
+  bool graphs = true;          // replay repeated forwards as CUDA graphs (S2S_GRAPHS=0: off)
   long long stop_after = -1;   // diagnostics: launches per forward before stopping
   long long fwd_launches = 0;  // launches enqueued by the forward in flight
   // Row-band sharding (s2s_band_init / s2s_band_init_local): this handle's rank.
   int band_rank = 0, band_world = 1;
   void* nccl_comm = nullptr;                  // ncclComm_t
+  cudaStream_t side = nullptr;                // halo transfers overlapping the QKV GEMM
+  cudaEvent_t fork = nullptr, join = nullptr;
   std::shared_ptr<s2s::LocalGroup> group;     // in-process group instead of NCCL
 };
 
@@ -401,6 +411,8 @@ void* dalloc(Plan& P, size_t bytes) {
 }
 
 void free_plan(Plan& P) {
+  if (P.gexec) cudaGraphExecDestroy(P.gexec);
+  P.gexec = nullptr;
   for (void* p : P.allocs) cudaFree(p);
   P.allocs.clear();
 }
@@ -563,6 +575,11 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
   ok &= make_map_rows(&P->mF0h, P->F0h + P->own_off * Cp, P->M_own, Cp, 128);
   ok &= make_map_rows(&P->mX16, P->X16 + P->own_off * Cp, P->M_own, Cp, 128);
   ok &= make_map_rows(&P->mX16s, P->X16 + P->sh_off * Cp, P->M_sh, Cp, 128);
+  if (band) {
+    ok &= make_map_rows(&P->mX16t, P->X16 + P->sh_off * Cp, (uint64_t)4 * wp, Cp, 128);
+    ok &= make_map_rows(&P->mX16b, P->X16 + (P->own_off + P->M_own) * Cp, (uint64_t)4 * wp, Cp,
+                        128);
+  }
   ok &= make_map_rows(&P->mAO, P->AO + P->own_off * Cp, P->M_own, Cp, 128);
   if (P->H16) ok &= make_map_rows(&P->mH16, P->H16 + P->own_off * H->HIDp, P->M_own, H->HIDp, 128);
   {
@@ -626,7 +643,7 @@ struct Launcher {
   // A transfer between bands (NCCL's kernels or copies, not ours): timed like a
   // launch, not counted as one.
   template <typename F>
-  void comm(const char* name, F&& f) {
+  void comm(const char* name, cudaStream_t cs, F&& f) {
     if (H->stop_after >= 0 && H->fwd_launches >= H->stop_after) return;
     const bool timed = H->profiling && (H->prof_only.empty() ||
                                         strncmp(name, H->prof_only.c_str(), H->prof_only.size()) == 0);
@@ -634,11 +651,11 @@ struct Launcher {
     if (timed) {
       a = ev();
       b = ev();
-      ck(cudaEventRecord(a, st), "event");
+      ck(cudaEventRecord(a, cs), "event");
     }
     f();
     if (timed) {
-      ck(cudaEventRecord(b, st), "event");
+      ck(cudaEventRecord(b, cs), "event");
       H->prof_pending.push_back({name, a, b});
     }
   }
@@ -802,7 +819,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
   __half* const X16 = P->X16 + P->own_off * Cp;
   float* const S = P->S + P->own_off * Cp;
   auto exchange = [&](const char* name, __half* buf, int n, bool cyclic, bool zero_edges) {
-    L.comm(name, [&] { halo_exchange(H, P, buf, Cp, n, cyclic, zero_edges, st); });
+    L.comm(name, st, [&] { halo_exchange(H, P, buf, Cp, n, cyclic, zero_edges, st); });
   };
   // 1. pad + conv_first (fp32 body skip F0, fp16 operand F0h).
   if (!band) {
@@ -840,16 +857,29 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       Block& bl = stg.blocks[b];
       const int sh = (b % 2 == 1) ? c.window / 2 : 0;
       const int k = sh ? 1 : 0;
-      // the shifted windows reach 4 rows into each neighbouring band (cyclically)
-      if (band && sh) exchange("halo_shift", P->X16, 4, true, false);
-      {  // QKV
+      auto qkv = [&](const CUtensorMap& mA, size_t off, int rows) {
         Epi e = epi0();
         e.bias = bl.qkv.b;
-        e.o16 = P->QKV + (sh ? P->sh_off : P->own_off) * H->NQ;
+        e.o16 = P->QKV + off * H->NQ;
         e.ld16 = H->NQ;
-        GemmArgs a = gemm_args(sh ? P->M_sh : M, H->NQ, Cp, e);
-        const CUtensorMap& mA = sh ? P->mX16s : P->mX16;
+        GemmArgs a = gemm_args(rows, H->NQ, Cp, e);
         L.run("gemm_qkv", [&] { return launch_gemm(mA, bl.qkv.map, out_maps(P, a), a, bl.qkv.BN, st); });
+      };
+      if (band && sh) {
+        // The shifted windows reach 4 rows into each neighbouring band (cyclically).
+        // Those rows travel on the side stream while the owned rows' QKV runs; the
+        // halo rows' QKV follows their arrival.
+        ck(cudaEventRecord(H->fork, st), "fork");
+        ck(cudaStreamWaitEvent(H->side, H->fork, 0), "fork");
+        L.comm("halo_shift", H->side,
+               [&] { halo_exchange(H, P, P->X16, Cp, 4, true, false, H->side); });
+        ck(cudaEventRecord(H->join, H->side), "join");
+        qkv(P->mX16, P->own_off, M);
+        ck(cudaStreamWaitEvent(st, H->join, 0), "join");
+        qkv(P->mX16t, P->sh_off, 4 * wp);
+        qkv(P->mX16b, P->own_off + M, 4 * wp);
+      } else {
+        qkv(P->mX16, P->own_off, M);
       }
       L.run("window_attention", [&] {
         return launch_window_attention(P->QKV, P->AO, bl.cpb, bl.ls, P->rows[k], P->nwin[k],
@@ -1105,6 +1135,63 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
   }
 }
 
+// forward_device, replayed from a CUDA graph when the same plan and I/O pointers
+// come back: the first forward runs eagerly (and sets up every kernel), the second
+// is captured on the handle's stream and launched, later ones only launch. Eager
+// always under the profiler, a debug stop, or an in-process band group (whose
+// exchange synchronises on the host).
+void run_forward(s2s_handle* H, int B, int h, int w, const float* d_in, float* d_out,
+                 float* d_aux, cudaStream_t st) {
+  if (!H->graphs || H->profiling || H->stop_after >= 0 || H->group) {
+    forward_device(H, B, h, w, d_in, d_out, d_aux, st);
+    return;
+  }
+  Plan* P = get_plan(H, B, h, w);
+  if (P->g_in != d_in || P->g_out != d_out || P->g_aux != d_aux) {
+    if (P->gexec) cudaGraphExecDestroy(P->gexec);
+    P->gexec = nullptr;
+    P->g_in = d_in;
+    P->g_out = d_out;
+    P->g_aux = d_aux;
+    P->g_seen = 0;
+  }
+  if (P->gexec) {
+    ck(cudaGraphLaunch(P->gexec, st), "graph launch");
+    H->launches += P->g_launches;
+    return;
+  }
+  if (P->g_seen++ == 0) {
+    forward_device(H, B, h, w, d_in, d_out, d_aux, st);
+    return;
+  }
+  // capture on the handle's own (non-blocking) stream, ordered after `st`
+  cudaEvent_t e0 = nullptr;
+  ck(cudaEventCreateWithFlags(&e0, cudaEventDisableTiming), "graph event");
+  cudaStream_t cs = H->stream;
+  ck(cudaEventRecord(e0, st), "graph event");
+  ck(cudaStreamWaitEvent(cs, e0, 0), "graph event");
+  cudaEventDestroy(e0);
+  ck(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal), "graph capture");
+  const long long l0 = H->launches;
+  cudaGraph_t g = nullptr;
+  try {
+    forward_device(H, B, h, w, d_in, d_out, d_aux, cs);
+  } catch (...) {
+    cudaStreamEndCapture(cs, &g);
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    throw;
+  }
+  ck(cudaStreamEndCapture(cs, &g), "graph capture");
+  const cudaError_t ie = cudaGraphInstantiate(&P->gexec, g, 0);
+  cudaGraphDestroy(g);
+  ck(ie, "graph instantiate");
+  P->g_launches = H->launches - l0;
+  H->launches = l0;
+  ck(cudaGraphLaunch(P->gexec, st), "graph launch");
+  H->launches += P->g_launches;
+}
+
 void check_device_error(s2s_handle* H) {
   unsigned int e = 0;
   ck(cudaMemcpyFromSymbol(&e, g_s2s_err, sizeof e), "error word");
@@ -1160,6 +1247,11 @@ const char* const kBandHandle =
 // Leave band mode: destroy the communicator / leave the group (the plan is rebuilt
 // for the new geometry on the next forward).
 void release_band(s2s_handle* H) {
+  if (H->plan) {  // its graph may hold the communicator's work
+    cudaStreamSynchronize(H->stream);
+    free_plan(*H->plan);
+    H->plan.reset();
+  }
   if (H->nccl_comm) {
     const NcclApi& api = nccl_api();
     if (api.ok) api.CommDestroy((ncclComm_t)H->nccl_comm);
@@ -1168,6 +1260,13 @@ void release_band(s2s_handle* H) {
   H->group.reset();
   H->band_rank = 0;
   H->band_world = 1;
+}
+
+// The side stream and fork/join events band forwards use (once per handle).
+void ensure_side(s2s_handle* H) {
+  if (!H->side) ck(cudaStreamCreateWithFlags(&H->side, cudaStreamNonBlocking), "side stream");
+  if (!H->fork) ck(cudaEventCreateWithFlags(&H->fork, cudaEventDisableTiming), "event");
+  if (!H->join) ck(cudaEventCreateWithFlags(&H->join, cudaEventDisableTiming), "event");
 }
 
 // Output rows [r0, r1) of an h-row image that `rank` of `world` bands produces.
@@ -1224,6 +1323,8 @@ int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, 
   {
     const char* f = getenv("S2S_UNFUSED_MLP");  // validation switch: the two-GEMM MLP path
     if (f && *f && strcmp(f, "0") != 0) H->fused_mlp = false;
+    const char* g = getenv("S2S_GRAPHS");
+    if (g && strcmp(g, "0") == 0) H->graphs = false;
   }
   TensorTable T;
   for (int i = 0; i < n_tensors; i++) T.t[tensors[i].name] = &tensors[i];
@@ -1252,7 +1353,7 @@ int s2s_forward_device(s2s_handle* H, int batch, int height, int width, const fl
     if (H->band_world > 1) fail(S2S_ERR_INVALID, kBandHandle);
     if (H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX && !d_aux)
       fail(S2S_ERR_INVALID, "the pixelshuffle_aux head needs an aux buffer on the device path");
-    forward_device(H, batch, height, width, d_in, d_out, d_aux, st);
+    run_forward(H, batch, height, width, d_in, d_out, d_aux, st);
   });
 }
 
@@ -1270,7 +1371,7 @@ int s2s_forward_batch(s2s_handle* H, int batch, int height, int width, const flo
     ensure_staging(H, &H->h_out, &H->h_out_n, nout);
     if (has_aux) ensure_staging(H, &H->h_aux, &H->h_aux_n, naux);
     ck(cudaMemcpyAsync(H->h_in, in, nin * 4, cudaMemcpyHostToDevice, H->stream), "upload");
-    forward_device(H, batch, height, width, H->h_in, H->h_out, has_aux ? H->h_aux : nullptr,
+    run_forward(H, batch, height, width, H->h_in, H->h_out, has_aux ? H->h_aux : nullptr,
                    H->stream);
     ck(cudaMemcpyAsync(out, H->h_out, nout * 4, cudaMemcpyDeviceToHost, H->stream), "download");
     if (has_aux && aux)
@@ -1421,6 +1522,7 @@ int s2s_band_init(s2s_handle* H, int rank, int world, const void* id, int id_byt
       const ncclResult_t r = api.CommInitRank(&comm, world, uid, rank);
       if (r != ncclSuccess) fail(S2S_ERR_NCCL, std::string("ncclCommInitRank: ") + api.GetErrorString(r));
       H->nccl_comm = comm;
+      ensure_side(H);
     }
     H->band_rank = rank;
     H->band_world = world;
@@ -1446,6 +1548,7 @@ int s2s_band_init_local(s2s_handle** hs, int world) {
         fail(S2S_ERR_UNSUPPORTED, "the pixelshuffle_aux head has no band mode");
       ck(cudaStreamSynchronize(H->stream), "band init");
       G->device[i] = H->device;
+      ensure_side(H);
       ck(cudaEventCreateWithFlags(&G->ready[i], cudaEventDisableTiming), "band event");
       ck(cudaEventCreateWithFlags(&G->done[i], cudaEventDisableTiming), "band event");
     });
@@ -1495,7 +1598,7 @@ int s2s_forward_band(s2s_handle* H, int height, int width, const float* d_in, fl
                      void* stream) {
   if (!H || !d_in || !d_out) return S2S_ERR_INVALID;
   cudaStream_t st = stream ? (cudaStream_t)stream : H->stream;
-  return guarded(H, [&] { forward_device(H, 1, height, width, d_in, d_out, nullptr, st); });
+  return guarded(H, [&] { run_forward(H, 1, height, width, d_in, d_out, nullptr, st); });
 }
 
 int s2s_forward_band_host(s2s_handle* H, int height, int width, const float* in, float* out) {
@@ -1509,7 +1612,7 @@ int s2s_forward_band_host(s2s_handle* H, int height, int width, const float* in,
     ensure_staging(H, &H->h_in, &H->h_in_n, nin);
     ensure_staging(H, &H->h_out, &H->h_out_n, std::max(nout, (size_t)1));
     ck(cudaMemcpyAsync(H->h_in, in, nin * 4, cudaMemcpyHostToDevice, H->stream), "upload");
-    forward_device(H, 1, height, width, H->h_in, H->h_out, nullptr, H->stream);
+    run_forward(H, 1, height, width, H->h_in, H->h_out, nullptr, H->stream);
     if (nout)
       ck(cudaMemcpyAsync(out, H->h_out, nout * 4, cudaMemcpyDeviceToHost, H->stream), "download");
     ck(cudaStreamSynchronize(H->stream), "forward");
@@ -1530,6 +1633,9 @@ void s2s_destroy(s2s_handle* H) {
   if (H->h_in) cudaFree(H->h_in);
   if (H->h_out) cudaFree(H->h_out);
   if (H->h_aux) cudaFree(H->h_aux);
+  if (H->side) cudaStreamDestroy(H->side);
+  if (H->fork) cudaEventDestroy(H->fork);
+  if (H->join) cudaEventDestroy(H->join);
   if (H->stream) cudaStreamDestroy(H->stream);
   delete H;
 }

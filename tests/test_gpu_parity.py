@@ -111,6 +111,36 @@ def test_forward_is_deterministic():
     assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("task", ["classical_sr", "real_sr"])
+def test_graph_replay_equals_the_eager_forward(task):
+    """Forward 1 runs eagerly, forward 2 is captured as a CUDA graph and launched,
+    forwards 3 and 4 replay it: all four outputs are identical, each forward counts
+    the same kernel launches, and new I/O pointers (another size) start over."""
+    capi = importlib.import_module("swin2sr_b200.capi")
+    P = pkg()
+    wt = P.weights.Weights.seeded(task, 0, True)
+    H = capi.Handle(wt)
+    try:
+        x = adjust(wt, np.random.default_rng(8).random((1, 3, 30, 41), dtype=np.float32))
+        outs, counts = [], []
+        for _ in range(4):
+            n0 = H.launch_count()
+            outs.append(H.forward_batch(x)[0])
+            counts.append(H.launch_count() - n0)
+        for o in outs[1:]:
+            assert np.array_equal(o, outs[0])
+        assert len(set(counts)) == 1 and counts[0] > 0, counts
+        y = adjust(wt, np.random.default_rng(9).random((1, 3, 17, 23), dtype=np.float32))
+        a = H.forward_batch(y)[0]
+        b = H.forward_batch(y)[0]
+        c = H.forward_batch(y)[0]
+        assert np.array_equal(a, b) and np.array_equal(a, c)
+        ref = oracle().forward(wt, 17, 23, y[0])[0]
+        assert float(np.abs(c[0] - ref.reshape(c[0].shape)).max()) <= TOL
+    finally:
+        H.close()
+
+
 def test_errors_are_reported_not_crashed():
     capi = importlib.import_module("swin2sr_b200.capi")
     wt, gpu = backend_for("lightweight_sr", 0, True)
