@@ -187,7 +187,8 @@ int s2s_band_halo_ops(int rank, int world, int own_rows, int rows, int cyclic, i
  * holding S2S_NOALLOC_MAX_TOKENS rows (4 MiB); batch * hp * wp above that is
  * rejected with S2S_ERR_INVALID. d_qkv is [batch*hp*wp][3*heads*dp] fp16 in image
  * order, per token [head][q|k|v][dp] with dp = head_dim rounded up to 16 (16-byte
- * aligned); d_out is [batch*hp*wp][ld_out] fp16, of which columns [0, embed) are
+ * aligned), as the forward's QKV projection writes it: q and k L2-normalised, q
+ * times exp(min(logit_scale, ln 100)) * log2(e); d_out is [batch*hp*wp][ld_out] fp16, of which columns [0, embed) are
  * written. hp and wp are the padded plane (multiples of the window); odd blocks
  * use the shifted window grid. Work is enqueued on `stream` (NULL = the handle's
  * stream) without synchronising. The first call on each device looks up the

@@ -7,12 +7,13 @@
 // table ([HPC][64][72] fp32, rows padded for conflict-free reads) is brought into
 // shared memory once; the producer gathers each window's q/k/v rows of those heads by
 // bulk copies into one of two buffers (full/empty mbarriers), so the next window's
-// copies overlap this window's math. Each compute warp derives the reciprocal L2 norms
-// it needs from the same fp16 values the MMAs read, then:
+// copies overlap this window's math. The QKV projection's epilogue has already
+// L2-normalised q and k and scaled q by exp(min(logit_scale, ln 100)) * log2 e, and the
+// bias table is stored times log2 e, so per window and head:
 //   S = Q K^T          mma.sync m16n8k16 fp16 -> fp32 (16 x 64 per warp, in registers)
-//   s = S * (1/|q|) * (1/|k|) * exp(min(logit_scale, ln 100)) + cpb[h][q][k]  (- 100 across shift
-//       regions; the region of a token is computed from its rolled plane coordinate)
-//   softmax along the row in registers (quad shuffles), max-subtracted
+//   t = S + cpb[h][q][k]   (- 100 log2 e across shift regions, in the last window row
+//       and column only; a token's region comes from its rolled plane coordinate)
+//   softmax along the row in registers (quad shuffles), max-subtracted, by exp2
 //   O = P V            mma.sync, P re-used from the S accumulators as fp16 A fragments
 //   out[token][h*hd + d] = O / rowsum
 // The residual stream and every token-row buffer stay in image order; this kernel
@@ -55,6 +56,13 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// 2^x by the SFU (the instruction __expf is built on, without its scaling multiply).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ int region_of(int a, int p, int win, int shift) {
   return (a + win < p) ? 0 : (a + shift < p) ? 1 : 2;
 }
@@ -72,7 +80,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 template <int DP, int HPC>
 __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     const __half* __restrict__ qkv, __half* __restrict__ out, const float* __restrict__ cpb,
-    const float* __restrict__ lscale, const int* __restrict__ rows, int heads, int hd, int ld_out,
+    const int* __restrict__ rows, int heads, int hd, int ld_out,
     int nwh, int nww, int hp, int wp, int shift, int nwin_total, int wh_off) {
   constexpr int N = 64;
   constexpr int NS = N + 8;                    // padded bias row (floats)
@@ -132,53 +140,28 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
   const int h = h0 + hl;
   const int qr0 = rb * 16 + g, qr1 = qr0 + 8;
   const int qoff = hl * 3 * DP, koff = qoff + DP, voff = qoff + 2 * DP;
-  const float ls = lscale[h];
   const float* cp0 = scpb + ((size_t)hl * N + qr0) * NS;
   const float* cp1 = scpb + ((size_t)hl * N + qr1) * NS;
   const uint32_t sbase0 = smem_u32(sqb);
   bool ok = mbar_wait(cbar, 0, DEV_TIMEOUT_FULL);
-  auto inv_norm = [&](const __half* p) {
-    const uint4* v = reinterpret_cast<const uint4*>(p);
-    float acc[DP / 8];
-#pragma unroll
-    for (int k = 0; k < DP / 8; k++) {
-      const uint4 u = v[k];
-      const __half2* h2 = reinterpret_cast<const __half2*>(&u);
-      float a = 0.0f;
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const float2 f = __half22float2(h2[e]);
-        a += f.x * f.x;
-        a += f.y * f.y;
-      }
-      acc[k] = a;
-    }
-    float sum = 0.0f;
-#pragma unroll
-    for (int k = 0; k < DP / 8; k++) sum += acc[k];
-    return 1.0f / fmaxf(sqrtf(sum), 1e-12f);
-  };
+  const int nwh_g = hp / 8;                   // window rows of the rolled plane
+  constexpr float kMask = -100.0f * 1.4426950408889634f;  // -100, in the exp2 domain
 
   int i = 0;
   for (int win = win0; win < nwin_total && ok; win += wstep, i++) {
     const int b = i & 1;
     if (!mbar_wait(&full[b], (i >> 1) & 1, DEV_TIMEOUT_FULL)) break;
-    const __half* sq = sqb + (size_t)b * N * SSTRIDE;
     const uint32_t sbase = sbase0 + (uint32_t)(b * N * SSTRIDE * 2);
     const int wi = win % nw;
     // window row on the (global) hp x wp plane the shift mask is defined on
     int wh = wi / nww + wh_off;
-    if (wh < 0) wh += hp / 8;
+    if (wh < 0) wh += nwh_g;
     const int ww = wi % nww;
     const size_t tok0 = (size_t)win * N;
-
-    // 1/|k| for keys lane and lane+32, 1/|q| for this thread's two query rows.
-    const float kn_lo = inv_norm(sq + (size_t)lane * SSTRIDE + koff);
-    const float kn_hi = inv_norm(sq + (size_t)(32 + lane) * SSTRIDE + koff);
-    const float qs0 = inv_norm(sq + (size_t)qr0 * SSTRIDE + qoff) * ls;
-    const float qs1 = inv_norm(sq + (size_t)qr1 * SSTRIDE + qoff) * ls;
+    // Only the last window row and column of a shifted block mix roll regions.
+    const bool masked = shift && (wh == nwh_g - 1 || ww == nww - 1);
     int qreg0 = 0, qreg1 = 0;
-    if (shift) {
+    if (masked) {
       qreg0 = 3 * region_of(wh * 8 + qr0 / 8, hp, 8, shift) + region_of(ww * 8 + qr0 % 8, wp, 8, shift);
       qreg1 = 3 * region_of(wh * 8 + qr1 / 8, hp, 8, shift) + region_of(ww * 8 + qr1 % 8, wp, 8, shift);
     }
@@ -204,28 +187,26 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
       }
     }
 
-    // Scale, bias, mask, softmax.
+    // Bias, mask, softmax (q and k arrive normalised, q scaled by the clamped logit
+    // scale times log2 e; the bias table is pre-scaled by log2 e).
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       const int k = 8 * j + 2 * t4;
-      // key k lives in lane k % 32 (low half for j < 4, high half otherwise)
-      const float ki0 = __shfl_sync(0xffffffffu, j < 4 ? kn_lo : kn_hi, k & 31);
-      const float ki1 = __shfl_sync(0xffffffffu, j < 4 ? kn_lo : kn_hi, (k + 1) & 31);
       const float2 b0 = *reinterpret_cast<const float2*>(cp0 + k);
       const float2 b1 = *reinterpret_cast<const float2*>(cp1 + k);
-      float s00 = sacc[j][0] * ki0 * qs0 + b0.x;
-      float s01 = sacc[j][1] * ki1 * qs0 + b0.y;
-      float s10 = sacc[j][2] * ki0 * qs1 + b1.x;
-      float s11 = sacc[j][3] * ki1 * qs1 + b1.y;
-      if (shift) {
+      float s00 = sacc[j][0] + b0.x;
+      float s01 = sacc[j][1] + b0.y;
+      float s10 = sacc[j][2] + b1.x;
+      float s11 = sacc[j][3] + b1.y;
+      if (masked) {
         const int kr0 = 3 * region_of(wh * 8 + k / 8, hp, 8, shift) + region_of(ww * 8 + k % 8, wp, 8, shift);
         const int kr1 = 3 * region_of(wh * 8 + (k + 1) / 8, hp, 8, shift) +
                         region_of(ww * 8 + (k + 1) % 8, wp, 8, shift);
-        if (qreg0 != kr0) s00 -= 100.0f;
-        if (qreg0 != kr1) s01 -= 100.0f;
-        if (qreg1 != kr0) s10 -= 100.0f;
-        if (qreg1 != kr1) s11 -= 100.0f;
+        if (qreg0 != kr0) s00 += kMask;
+        if (qreg0 != kr1) s01 += kMask;
+        if (qreg1 != kr0) s10 += kMask;
+        if (qreg1 != kr1) s11 += kMask;
       }
       sacc[j][0] = s00;
       sacc[j][1] = s01;
@@ -241,10 +222,10 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     float sum0 = 0.0f, sum1 = 0.0f;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      sacc[j][0] = __expf(sacc[j][0] - mx0);
-      sacc[j][1] = __expf(sacc[j][1] - mx0);
-      sacc[j][2] = __expf(sacc[j][2] - mx1);
-      sacc[j][3] = __expf(sacc[j][3] - mx1);
+      sacc[j][0] = ex2(sacc[j][0] - mx0);
+      sacc[j][1] = ex2(sacc[j][1] - mx0);
+      sacc[j][2] = ex2(sacc[j][2] - mx1);
+      sacc[j][3] = ex2(sacc[j][3] - mx1);
       sum0 += sacc[j][0] + sacc[j][1];
       sum1 += sacc[j][2] + sacc[j][3];
     }
@@ -293,7 +274,7 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
 }
 
 template <int DP, int HPC>
-cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb, const float* lscale,
+cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb,
                           const int* rows, int nwin_total, int heads, int hd, int ld_out, int nwh,
                           int nww, int hp, int wp, int shift, int wh_off, cudaStream_t st) {
   constexpr int SEG = HPC * 3 * DP;
@@ -318,28 +299,28 @@ cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb, cons
   G = (G / NG) * NG;
   if (G < NG) G = NG;
   k_window_attention<DP, HPC><<<(unsigned)G, 128 * HPC + 32, smem, st>>>(
-      qkv, out, cpb, lscale, rows, heads, hd, ld_out, nwh, nww, hp, wp, shift, nwin_total, wh_off);
+      qkv, out, cpb, rows, heads, hd, ld_out, nwh, nww, hp, wp, shift, nwin_total, wh_off);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
-                                    const float* lscale, const int* rows, int nwin_total,
+                                    const int* rows, int nwin_total,
                                     int heads, int hd, int dp, int ld_out, int nwh, int nww,
                                     int hp, int wp, int shift, int wh_off, cudaStream_t st) {
   const bool pair = heads % 2 == 0;
   if (dp == 32 && pair)
-    return launch_attn_t<32, 2>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
+    return launch_attn_t<32, 2>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
                                 nww, hp, wp, shift, wh_off, st);
   if (dp == 32)
-    return launch_attn_t<32, 1>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
+    return launch_attn_t<32, 1>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
                                 nww, hp, wp, shift, wh_off, st);
   if (dp == 16 && pair)
-    return launch_attn_t<16, 2>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
+    return launch_attn_t<16, 2>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
                                 nww, hp, wp, shift, wh_off, st);
   if (dp == 16)
-    return launch_attn_t<16, 1>(qkv, out, cpb, lscale, rows, nwin_total, heads, hd, ld_out, nwh,
+    return launch_attn_t<16, 1>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
                                 nww, hp, wp, shift, wh_off, st);
   return cudaErrorInvalidValue;
 }

@@ -33,7 +33,7 @@
 
 namespace s2s {
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
-                                    const float* lscale, const int* rows, int nwin_total,
+                                    const int* rows, int nwin_total,
                                     int heads, int hd, int dp, int ld_out, int nwh, int nww,
                                     int hp, int wp, int shift, int wh_off, cudaStream_t st);
 cudaError_t launch_pad_reflect(const float* x, float* y, int B, int c, int h, int w, int hp,
@@ -82,7 +82,8 @@ struct TcWeight {
 
 struct Block {
   TcWeight qkv, proj, fc1, fc2;
-  float *n1g, *n1b, *n2g, *n2b, *cpb, *ls;
+  float *n1g, *n1b, *n2g, *n2b;
+  float *cpb, *ls;  // bias table and q scale, both times log2 e (attention softmax is exp2)
 };
 
 struct Stage {
@@ -326,18 +327,20 @@ void build_weights(s2s_handle* H, const TensorTable& T) {
       bl.n2b = upload(H, padded(T.get(p + "norm2.bias", C), C, Cp));
       // cpb_pre [N*N][heads] -> [heads][N][N + 8] (rows padded so that the attention
       // kernel's shared-memory reads are free of bank conflicts); logit scale ->
-      // exp(min(ls, ln 100)).
+      // exp(min(ls, ln 100)). Both times log2 e: the attention kernel's softmax is exp2.
+      const float kLog2e = 1.4426950408889634f;
       const float* cpb = T.get(p + "attn.cpb_pre", (int64_t)n * n * heads);
       const int ns = n + 8;
       std::vector<float> cpbt((size_t)heads * n * ns, 0.0f);
       for (int q = 0; q < n; q++)
         for (int k = 0; k < n; k++)
           for (int h = 0; h < heads; h++)
-            cpbt[((size_t)h * n + q) * ns + k] = cpb[((size_t)q * n + k) * heads + h];
+            cpbt[((size_t)h * n + q) * ns + k] = cpb[((size_t)q * n + k) * heads + h] * kLog2e;
       bl.cpb = upload(H, cpbt);
       const float* ls = T.get(p + "attn.logit_scale", heads);
       std::vector<float> lse(heads);
-      for (int h = 0; h < heads; h++) lse[h] = std::exp(std::fmin(ls[h], std::log(100.0f)));
+      for (int h = 0; h < heads; h++)
+        lse[h] = std::exp(std::fmin(ls[h], std::log(100.0f))) * kLog2e;
       bl.ls = upload(H, lse);
     }
     char cn[64], pn[64], cb[64], pb[64];
@@ -860,6 +863,9 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       auto qkv = [&](const CUtensorMap& mA, size_t off, int rows) {
         Epi e = epi0();
         e.bias = bl.qkv.b;
+        e.act = ACT_QKNORM;  // normalised q (times the logit scale) and k for the attention
+        e.qk_scale = bl.ls;
+        e.qk_dp = H->DP;
         e.o16 = P->QKV + off * H->NQ;
         e.ld16 = H->NQ;
         GemmArgs a = gemm_args(rows, H->NQ, Cp, e);
@@ -882,7 +888,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         qkv(P->mX16, P->own_off, M);
       }
       L.run("window_attention", [&] {
-        return launch_window_attention(P->QKV, P->AO, bl.cpb, bl.ls, P->rows[k], P->nwin[k],
+        return launch_window_attention(P->QKV, P->AO, bl.cpb, P->rows[k], P->nwin[k],
                                        H->heads, H->hd, H->DP, Cp, P->nwh_l[k], wp / 8, P->ghp,
                                        wp, sh, P->wh_off[k], st);
       });

@@ -339,6 +339,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           v[4 * u + 3] = x[3];
           if (e.o32 || e.o32b) *slot = make_float4(x[0], x[1], x[2], x[3]);
         }
+        if constexpr (ACT == ACT_QKNORM) {
+          // one head's q, k or v is one DP-wide group of this row's columns
+          auto group_scale = [&](int grp, float ss) {
+            const int part = grp % 3;
+            const float r = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+            return part == 0 ? r * e.qk_scale[grp / 3] : part == 1 ? r : 1.0f;
+          };
+          const int gc = n0 + cl0;
+          if (e.qk_dp == 32) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; j++) ss = fmaf(v[j], v[j], ss);
+            const float sc = group_scale(gc / 32, ss);
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] *= sc;
+          } else {
+            float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+              s0 = fmaf(v[j], v[j], s0);
+              s1 = fmaf(v[16 + j], v[16 + j], s1);
+            }
+            const float c0 = group_scale(gc / 16, s0), c1 = group_scale(gc / 16 + 1, s1);
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+              v[j] *= c0;
+              v[16 + j] *= c1;
+            }
+          }
+        }
         if (e.o16) {
 #pragma unroll
           for (int u = 0; u < 4; u++) {
@@ -539,6 +569,9 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   const Epi& e = a.epi;
   if (e.ln_n > 0 && a.N != BN) return cudaErrorInvalidValue;
   if (e.res_pre && e.res_post) return cudaErrorInvalidValue;
+  if (e.act == ACT_QKNORM && (e.o32 || e.o32b || e.ln_n || !e.qk_scale ||
+                              (e.qk_dp != 16 && e.qk_dp != 32) || a.N % (3 * e.qk_dp)))
+    return cudaErrorInvalidValue;
   const int act = e.act;
   const bool ln = e.ln_n > 0;
   const int res = e.res_pre ? 1 : (e.res_post ? 2 : 0);
@@ -551,6 +584,8 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   S2S_VARIANT(192, 3, ACT_NONE, false, 1, STORE_ROWS)
   S2S_VARIANT(192, 3, ACT_NONE, true, 1, STORE_ROWS)
   S2S_VARIANT(192, 3, ACT_NONE, false, 2, STORE_ROWS)
+  S2S_VARIANT(192, 3, ACT_QKNORM, false, 0, STORE_ROWS)
+  S2S_VARIANT(96, 4, ACT_QKNORM, false, 0, STORE_ROWS)
   // embed 60 (Cp 64) and the 64-channel head convs
   S2S_VARIANT(64, 4, ACT_NONE, false, 0, STORE_ROWS)
   S2S_VARIANT(64, 4, ACT_NONE, true, 2, STORE_ROWS)

@@ -7,7 +7,11 @@
 
 namespace s2s {
 
-enum Act : int { ACT_NONE = 0, ACT_GELU = 1, ACT_LRELU = 2 };
+// ACT_QKNORM: the QKV projection's epilogue. Columns are [head][q|k|v][qk_dp]; q and k
+// groups are L2-normalised per row (F.normalize, eps 1e-12) and q is further scaled by
+// qk_scale[head] (the clamped logit scale times log2 e), so the attention kernel's
+// logits are one dot product in the exp2 domain.
+enum Act : int { ACT_NONE = 0, ACT_GELU = 1, ACT_LRELU = 2, ACT_QKNORM = 3 };
 
 // Where the epilogue writes.
 enum Store : int {
@@ -22,6 +26,8 @@ struct Epi {
   const float* bias;  // padded to the full N, or null
   int act;
   float slope;
+  const float* qk_scale;  // ACT_QKNORM: per head
+  int qk_dp;              // ACT_QKNORM: padded head dim (16 or 32)
   // fp32 residual added after the activation (before a LayerNorm), indexed by the
   // tile's logical row and the global column; thread-per-row reads.
   const float* res_pre;

@@ -2,6 +2,8 @@
 // input plane, the 3-input-channel convolutions (conv_first, conv_after_aux,
 // conv_bicubic), the bicubic resample of the compressed head, and the nearest
 // x2 upsample of the real-world head.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace s2s {
@@ -45,43 +47,88 @@ __global__ void k_pad_band(const float* __restrict__ x, float* __restrict__ y, i
 }
 
 // 3x3 s1 p1 conv with 3 input channels, NCHW fp32 input -> NHWC outputs.
-// Thread = (pixel, output channel), channel fastest, so stores are contiguous.
+// A warp is 32 consecutive pixels of one row and one group of 8 output channels:
+// the input loads coalesce across the warp, the weights are shared-memory
+// broadcasts, and each thread stores its pixel's 8 channels as 32 + 16 bytes.
 // Taps in the oracle's order: bias first, then ky, kx, ci.
-__global__ void k_conv3_small(const float* __restrict__ in, const float* __restrict__ wgt,
-                              const float* __restrict__ bias, int B, int H, int W, int co_n,
-                              int act, float slope, float* __restrict__ o32, int ld32,
-                              __half* __restrict__ o16, int ld16) {
-  __shared__ float sw[256 * 27];
-  __shared__ float sb[256];
-  for (int i = threadIdx.x; i < co_n * 27; i += blockDim.x) sw[i] = wgt[i];
-  for (int i = threadIdx.x; i < co_n; i += blockDim.x) sb[i] = bias[i];
+constexpr int kConvGroups = 8;  // channel groups per block (blockDim = 32 x 8)
+__global__ void __launch_bounds__(256) k_conv3_small(
+    const float* __restrict__ in, const float* __restrict__ wgt, const float* __restrict__ bias,
+    int B, int H, int W, int co_n, int act, float slope, float* __restrict__ o32, int ld32,
+    __half* __restrict__ o16, int ld16) {
+  __shared__ float sw[kConvGroups * 8][27];
+  __shared__ float sb[kConvGroups * 8];
+  const int lane = threadIdx.x, g = threadIdx.y;
+  const int cbase = blockIdx.y * kConvGroups * 8;
+  for (int i = g * 32 + lane; i < kConvGroups * 8 * 27; i += 256) {
+    const int co = cbase + i / 27;
+    sw[i / 27][i % 27] = co < co_n ? wgt[(size_t)co * 27 + i % 27] : 0.0f;
+  }
+  for (int i = g * 32 + lane; i < kConvGroups * 8; i += 256)
+    sb[i] = cbase + i < co_n ? bias[cbase + i] : 0.0f;
   __syncthreads();
-  const size_t n = (size_t)B * H * W * co_n;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const int co = (int)(i % co_n);
-    const size_t p = i / co_n;
-    const int x = (int)(p % W);
-    const int y = (int)((p / W) % H);
-    const int b = (int)(p / ((size_t)W * H));
-    float acc = sb[co];
-    const float* wc = sw + co * 27;
+  const int c0 = cbase + g * 8;  // this warp's first output channel
+  if (c0 >= co_n) return;
+  const int tiles_x = (W + 31) / 32;
+  const size_t ntiles = (size_t)B * H * tiles_x;
+  for (size_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const int tx = (int)(t % tiles_x);
+    const int y = (int)((t / tiles_x) % H);
+    const int b = (int)(t / ((size_t)tiles_x * H));
+    const int x = tx * 32 + lane;
+    if (x >= W) continue;
+    float v[27];
 #pragma unroll
-    for (int ky = 0; ky < 3; ky++) {
-      const int sy = y + ky - 1;
-      if (sy < 0 || sy >= H) continue;
+    for (int ci = 0; ci < 3; ci++)
 #pragma unroll
-      for (int kx = 0; kx < 3; kx++) {
-        const int sx = x + kx - 1;
-        if (sx < 0 || sx >= W) continue;
+      for (int ky = 0; ky < 3; ky++)
 #pragma unroll
-        for (int ci = 0; ci < 3; ci++)
-          acc += wc[ci * 9 + ky * 3 + kx] * in[(((size_t)b * 3 + ci) * H + sy) * W + sx];
-      }
+        for (int kx = 0; kx < 3; kx++) {
+          const int sy = y + ky - 1, sx = x + kx - 1;
+          v[ci * 9 + ky * 3 + kx] = (sy >= 0 && sy < H && sx >= 0 && sx < W)
+                                        ? in[(((size_t)b * 3 + ci) * H + sy) * W + sx]
+                                        : 0.0f;
+        }
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float* wc = sw[g * 8 + j];
+      float a = sb[g * 8 + j];
+#pragma unroll
+      for (int ky = 0; ky < 3; ky++)
+#pragma unroll
+        for (int kx = 0; kx < 3; kx++)
+#pragma unroll
+          for (int ci = 0; ci < 3; ci++) a += wc[ci * 9 + ky * 3 + kx] * v[ci * 9 + ky * 3 + kx];
+      if (act == 2 && a < 0.0f) a *= slope;
+      acc[j] = a;
     }
-    if (act == 2 && acc < 0.0f) acc *= slope;
-    if (o32) o32[p * ld32 + co] = acc;
-    if (o16) o16[p * ld16 + co] = __float2half_rn(acc);
+    const size_t p = ((size_t)b * H + y) * W + x;
+    const int nv = min(8, co_n - c0);
+    if (nv == 8) {
+      if (o32) {
+        float4* d = reinterpret_cast<float4*>(o32 + p * ld32 + c0);
+        d[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        d[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      }
+      if (o16) {
+        uint4 u;
+        __half2 h0 = __floats2half2_rn(acc[0], acc[1]), h1 = __floats2half2_rn(acc[2], acc[3]);
+        __half2 h2 = __floats2half2_rn(acc[4], acc[5]), h3 = __floats2half2_rn(acc[6], acc[7]);
+        u.x = *reinterpret_cast<uint32_t*>(&h0);
+        u.y = *reinterpret_cast<uint32_t*>(&h1);
+        u.z = *reinterpret_cast<uint32_t*>(&h2);
+        u.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(o16 + p * ld16 + c0) = u;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        if (j < nv) {
+          if (o32) o32[p * ld32 + c0 + j] = acc[j];
+          if (o16) o16[p * ld16 + c0 + j] = __float2half_rn(acc[j]);
+        }
+    }
   }
 }
 
@@ -177,9 +224,15 @@ cudaError_t launch_pad_band(const float* x, float* y, int c, int h, int w, int h
 cudaError_t launch_conv3_small(const float* in, const float* wgt, const float* bias, int B, int H,
                                int W, int co_n, int act, float slope, float* o32, int ld32,
                                __half* o16, int ld16, cudaStream_t st) {
-  if (co_n > 256) return cudaErrorInvalidValue;
-  k_conv3_small<<<grid_for((size_t)B * H * W * co_n, 256), 256, 0, st>>>(
-      in, wgt, bias, B, H, W, co_n, act, slope, o32, ld32, o16, ld16);
+  // vector stores: 8-channel groups start 32-byte (fp32) / 16-byte (fp16) aligned
+  if ((o32 && (ld32 % 4 || (uintptr_t)o32 % 16)) || (o16 && (ld16 % 8 || (uintptr_t)o16 % 16)))
+    return cudaErrorInvalidValue;
+  const int gy = (co_n + kConvGroups * 8 - 1) / (kConvGroups * 8);
+  const size_t tiles = (size_t)B * H * ((W + 31) / 32);
+  // a few blocks per SM, each walking many pixel tiles: the weight staging is paid once
+  const unsigned gx = (unsigned)std::min<size_t>(tiles, (size_t)148 * 3);
+  k_conv3_small<<<dim3(gx, gy), dim3(32, kConvGroups), 0, st>>>(in, wgt, bias, B, H, W, co_n, act,
+                                                                 slope, o32, ld32, o16, ld16);
   return cudaGetLastError();
 }
 
