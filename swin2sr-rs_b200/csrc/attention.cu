@@ -148,8 +148,20 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
   constexpr float kMask = -100.0f * 1.4426950408889634f;  // -100, in the exp2 domain
 
   int i = 0;
+  // this thread's two output rows of the first window (the next window's are loaded
+  // while this one computes)
+  int orow0 = 0, orow1 = 0;
+  if (win0 < nwin_total) {
+    orow0 = rows[(size_t)win0 * N + qr0];
+    orow1 = rows[(size_t)win0 * N + qr1];
+  }
   for (int win = win0; win < nwin_total && ok; win += wstep, i++) {
     const int b = i & 1;
+    const int cur0 = orow0, cur1 = orow1;
+    if (win + wstep < nwin_total) {
+      orow0 = rows[(size_t)(win + wstep) * N + qr0];
+      orow1 = rows[(size_t)(win + wstep) * N + qr1];
+    }
     if (!mbar_wait(&full[b], (i >> 1) & 1, DEV_TIMEOUT_FULL)) break;
     const uint32_t sbase = sbase0 + (uint32_t)(b * N * SSTRIDE * 2);
     const int wi = win % nw;
@@ -157,7 +169,6 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     int wh = wi / nww + wh_off;
     if (wh < 0) wh += nwh_g;
     const int ww = wi % nww;
-    const size_t tok0 = (size_t)win * N;
     // Only the last window row and column of a shifted block mix roll regions.
     const bool masked = shift && (wh == nwh_g - 1 || ww == nww - 1);
     int qreg0 = 0, qreg1 = 0;
@@ -258,8 +269,8 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[b]);
     const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
-    __half* o0 = out + (size_t)rows[tok0 + qr0] * ld_out + h * hd;
-    __half* o1 = out + (size_t)rows[tok0 + qr1] * ld_out + h * hd;
+    __half* o0 = out + (size_t)cur0 * ld_out + h * hd;
+    __half* o1 = out + (size_t)cur1 * ld_out + h * hd;
 #pragma unroll
     for (int n = 0; n < DP / 8; n++) {
       const int d = n * 8 + 2 * t4;

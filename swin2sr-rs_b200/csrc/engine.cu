@@ -78,6 +78,7 @@ struct TcWeight {
   float* b = nullptr;
   int N = 0, K = 0, BN = 0;
   CUtensorMap map;
+  CUtensorMap mlp_map;  // fc1 only: 64-row boxes, the fused MLP's hidden part
 };
 
 struct Block {
@@ -319,6 +320,8 @@ void build_weights(s2s_handle* H, const TensorTable& T) {
       pack_linear(H, bl.fc1, T.get(p + "mlp.fc1.weight", (int64_t)HID * C),
                   T.get(p + "mlp.fc1.bias", HID), C, HIDp, Cp, n_tile_for(HIDp),
                   identity_rows(HIDp, HID));
+      if (!make_map_rows(&bl.fc1.mlp_map, bl.fc1.w, (uint64_t)HIDp, (uint64_t)Cp, 64))
+        fail(S2S_ERR_CUDA, "cuTensorMapEncodeTiled failed for a weight operand");
       pack_linear(H, bl.fc2, T.get(p + "mlp.fc2.weight", (int64_t)C * HID),
                   T.get(p + "mlp.fc2.bias", C), HID, Cp, HIDp, Cp, identity_rows(Cp, C));
       bl.n1g = upload(H, padded(T.get(p + "norm1.weight", C), C, Cp));
@@ -926,7 +929,8 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
           eo.o16 = X16;
           eo.ld16 = Cp;
           const OutMaps om = out_maps(P, gemm_args(M, Cp, Cp, eo));
-          return launch_mlp(P->mX16, bl.fc1.map, bl.fc2.map, om.o32, om.o16, m, Cp, H->HIDp, st);
+          return launch_mlp(P->mX16, bl.fc1.mlp_map, bl.fc2.map, om.o32, om.o16, m, Cp, H->HIDp,
+                            st);
         });
       } else {
         {  // fc1 + GELU

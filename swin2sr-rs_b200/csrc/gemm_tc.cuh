@@ -97,9 +97,9 @@ struct MlpArgs {
   __half* x16;           // [M][CP] fp16 copy, updated in place
 };
 
-// mapX: rows map of x16 (box 128 rows); mapW1: fc1 weight [HP][CP] (box N1 rows);
+// mapX: rows map of x16 (box 128 rows); mapW1: fc1 weight [HP][CP] (box 64 rows);
 // mapW2: fc2 weight [CP][HP] (box CP rows); mapX32 / mapX16o: make_map_out_rows maps of
-// x (fp32, also the residual) and x16. Supported (cp, hp): (192, 384), (64, 128).
+// x (fp32) and x16. Supported (cp, hp): (192, 384), (64, 128).
 cudaError_t launch_mlp(const CUtensorMap& mapX, const CUtensorMap& mapW1,
                        const CUtensorMap& mapW2, const CUtensorMap& mapX32,
                        const CUtensorMap& mapX16o, const MlpArgs& a, int cp, int hp,
