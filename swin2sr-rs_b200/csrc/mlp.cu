@@ -11,17 +11,18 @@
 // The MMA warp issues fc1 part j+2 right after fc2 chunk j, so the tensor core always
 // has the next part queued while the epilogue warps run GELU, and with two D2
 // accumulators the next tile's parts start while this tile's epilogue 2 drains.
-// The hidden activation never leaves the SM. Roles as in gemm_tc.cu: warp 0 TMA,
-// warp 1 MMA + TMEM, warps 2..9 epilogue (two per TMEM lane quarter, 32 columns each
-// of a part). All waits are bounded.
+// The hidden activation never leaves the SM. Warp roles: warp 0 TMA, warp 1 MMA +
+// TMEM, warps 2..9 epilogue 1 (GELU), warps 10..17 epilogue 2 (LayerNorm +
+// residual) - the two epilogue groups work on consecutive tiles at the same time,
+// two warps per TMEM lane quarter each. All waits are bounded.
 #include "common.cuh"
 #include "gemm_tc.cuh"
 
 namespace s2s {
 namespace {
 
-constexpr int kMlpThreads = 320;
-constexpr int kMlpEpiWarps = 8;
+constexpr int kMlpThreads = 576;
+constexpr int kMlpEpiWarps = 8;  // per epilogue group
 constexpr int kMlpPart = 64;  // hidden columns per part
 
 template <int CP, int HP, int STAGES>
@@ -33,8 +34,11 @@ struct MlpCfg {
   static constexpr uint32_t TCOLS = TUSED <= 128 ? 128 : TUSED <= 256 ? 256 : 512;
   // a ring slot holds one fc1 part's weights (KC1 boxes of 64 x 64) or one fc2 chunk
   static constexpr int SLOT = KC1 * 8192 > CP * 128 ? KC1 * 8192 : CP * 128;
+  // epilogue 2 per warp: two fp32 32x32 tiles (residual in / result out, 128-byte
+  // swizzle) and one fp16 tile (64-byte swizzle)
+  static constexpr int STG = 2 * 4096 + 2048;
   static constexpr size_t SMEM = 1024 + (size_t)KC1 * 16384 + 2 * 16384 +
-                                 (size_t)STAGES * SLOT + (size_t)kMlpEpiWarps * 8192 +
+                                 (size_t)STAGES * SLOT + (size_t)kMlpEpiWarps * STG +
                                  (HP + 3 * CP) * 4 + (2 * STAGES + 12 + 2 * kMlpEpiWarps) * 8 + 16;
 };
 
@@ -48,16 +52,14 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   static_assert(HP % kMlpPart == 0 && CP % 64 == 0 && NP % 2 == 0, "tile shapes");
   static_assert(Cfg::TUSED <= 512, "TMEM columns");
   static_assert(Cfg::SMEM <= 232448, "shared memory");
-  // the fp16 output tiles of epilogue 2 live in the hidden chunk buffers
-  static_assert(2 * 16384 >= kMlpEpiWarps * 2 * 2048, "epilogue-2 fp16 staging");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sX = smem;                           // KC1 chunks: the X16 tile
   uint8_t* sH = sX + KC1 * 16384;               // 2 hidden chunk buffers (16 KB each)
   uint8_t* ring = sH + 2 * 16384;
-  uint8_t* f32buf = ring + STAGES * Cfg::SLOT;  // [kMlpEpiWarps][2][4096]
-  float* s_vec = reinterpret_cast<float*>(f32buf + kMlpEpiWarps * 8192);  // b1, b2, g2, beta2
+  uint8_t* stgbuf = ring + STAGES * Cfg::SLOT;  // [kMlpEpiWarps][STG] epilogue-2 staging
+  float* s_vec = reinterpret_cast<float*>(stgbuf + kMlpEpiWarps * Cfg::STG);  // b1, b2, g2, beta2
   uint64_t* full = reinterpret_cast<uint64_t*>(s_vec + HP + 3 * CP);
   uint64_t* empty = full + STAGES;
   uint64_t* acc1 = empty + STAGES;   // [2] fc1 part in D1 buffer b
@@ -66,8 +68,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   uint64_t* d2free = acc2 + 2;       // [2] D2 buffer d drained (8 warp arrivals)
   uint64_t* xfull = d2free + 2;      // X16 tile landed
   uint64_t* xfree = xfull + 1;       // fc1 of the tile retired: X16 buffer reusable
-  uint64_t* sfree = xfree + 1;       // epilogue-2 fp16 tiles read out (8 warp arrivals)
-  uint64_t* fin = sfree + 1;
+  uint64_t* fin = xfree + 2;
   uint64_t* rbar = fin + 1;          // [kMlpEpiWarps][2] residual tile landed
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rbar + 2 * kMlpEpiWarps);
 
@@ -92,7 +93,6 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     }
     mbar_init(xfull, 1);
     mbar_init(xfree, 1);
-    mbar_init(sfree, kMlpEpiWarps);
     mbar_init(fin, 1);
     for (int k = 0; k < 2 * kMlpEpiWarps; k++) mbar_init(&rbar[k], 1);
     fence_barrier_init();
@@ -229,160 +229,160 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogues
-    const int q = warp & 3;
-    const int half = (warp - 2) >> 2;  // which 32 columns of a part
+    const bool gelu_group = warp < 2 + kMlpEpiWarps;
+    const int gw = gelu_group ? warp - 2 : warp - 2 - kMlpEpiWarps;  // warp within its group
+    const int q = warp & 3;            // TMEM lane quarter
+    const int half = gw >> 2;          // which half of the columns
     const int et = threadIdx.x - 64;
     const int r = q * 32 + lane;       // tile row of this thread
-    for (int c = et; c < HP; c += 32 * kMlpEpiWarps) s_vec[c] = a.b1[c];
-    for (int c = et; c < CP; c += 32 * kMlpEpiWarps) {
+    for (int c = et; c < HP; c += 64 * kMlpEpiWarps) s_vec[c] = a.b1[c];
+    for (int c = et; c < CP; c += 64 * kMlpEpiWarps) {
       s_vec[HP + c] = a.b2[c];
       s_vec[HP + CP + c] = a.g2[c];
       s_vec[HP + 2 * CP + c] = a.beta2[c];
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(32 * kMlpEpiWarps) : "memory");
-    const int wq = warp - 2;
-    uint8_t* wf32 = f32buf + wq * 8192;
-    uint8_t* wf16 = sH + wq * 4096;  // in the hidden buffers, dead during epilogue 2
-    uint64_t* wrb = rbar + 2 * wq;
-    uint32_t jcnt = 0;
+    asm volatile("bar.sync 1, %0;" ::"r"(64 * kMlpEpiWarps) : "memory");
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
-    const int sw128 = lane & 7, sw64 = (lane >> 1) & 3;  // this row's swizzle phases
-    int i = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
-      const int row0 = t * 128 + q * 32;  // this warp's 32 rows as a TMA box origin
+    if (gelu_group) {
       // ---- epilogue 1: hidden chunk j = GELU(D1 + b1) -> fp16 -> shared
-      for (int j = 0; j < NP; j++) {
-        const uint32_t ph = (uint32_t)((i * (NP / 2) + (j >> 1)) & 1);
-        if (!mbar_wait(&acc1[j & 1], ph, DEV_TIMEOUT_ACC)) {
-          ok = false;
-          break;
-        }
-        // the previous tile's epilogue-2 fp16 tiles sat in the hidden buffers
-        if (j == 0 && i > 0 && !mbar_wait(sfree, (i - 1) & 1, DEV_TIMEOUT_ACC)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        float v[32];
-        tmem_ld32(tq + (uint32_t)((j & 1) * kMlpPart + half * 32), v);
-        const int col0 = j * kMlpPart + half * 32;  // hidden column of v[0]
-        uint32_t hv[16];
+      int i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
+        for (int j = 0; j < NP; j++) {
+          const uint32_t ph = (uint32_t)((i * (NP / 2) + (j >> 1)) & 1);
+          if (!mbar_wait(&acc1[j & 1], ph, DEV_TIMEOUT_ACC)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          float v[32];
+          tmem_ld32(tq + (uint32_t)((j & 1) * kMlpPart + half * 32), v);
+          const int col0 = j * kMlpPart + half * 32;  // hidden column of v[0]
+          uint32_t hv[16];
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const float4 bb = *reinterpret_cast<const float4*>(s_vec + col0 + 4 * u);
-          const __half2 h0 = __floats2half2_rn(gelu_erf(v[4 * u] + bb.x), gelu_erf(v[4 * u + 1] + bb.y));
-          const __half2 h1 = __floats2half2_rn(gelu_erf(v[4 * u + 2] + bb.z), gelu_erf(v[4 * u + 3] + bb.w));
-          hv[2 * u] = *reinterpret_cast<const uint32_t*>(&h0);
-          hv[2 * u + 1] = *reinterpret_cast<const uint32_t*>(&h1);
-        }
-        uint8_t* chunk = sH + (j & 1) * 16384;
+          for (int u = 0; u < 8; u++) {
+            const float4 bb = *reinterpret_cast<const float4*>(s_vec + col0 + 4 * u);
+            const __half2 h0 = __floats2half2_rn(gelu_erf(v[4 * u] + bb.x), gelu_erf(v[4 * u + 1] + bb.y));
+            const __half2 h1 = __floats2half2_rn(gelu_erf(v[4 * u + 2] + bb.z), gelu_erf(v[4 * u + 3] + bb.w));
+            hv[2 * u] = *reinterpret_cast<const uint32_t*>(&h0);
+            hv[2 * u + 1] = *reinterpret_cast<const uint32_t*>(&h1);
+          }
+          uint8_t* chunk = sH + (j & 1) * 16384;
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int uu = (half * 4 + u) ^ (r & 7);
-          *reinterpret_cast<uint4*>(chunk + r * 128 + uu * 16) =
-              make_uint4(hv[4 * u], hv[4 * u + 1], hv[4 * u + 2], hv[4 * u + 3]);
-        }
-        // generic-proxy writes -> visible to the tensor core (async proxy); the D1
-        // buffer is drained
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&hfull[j & 1]);
-      }
-      if (!ok) break;
-      // ---- epilogue 2: X <- X + LN2(D2 + b2), X16 <- fp16(X), through TMA
-      const int db = i & 1;
-      const uint32_t td2 = tq + (uint32_t)(Cfg::D2OFF + db * CP);
-      // the first residual tile is requested before waiting for fc2
-      if (lane == 0 && half < CP / 32) {
-        bulk_wait_read<0>();
-        mbar_arrive_expect_tx(&wrb[jcnt & 1], 4096);
-        tma_load_2d(wf32 + (jcnt & 1) * 4096, &mapX32, &wrb[jcnt & 1], half * 32, row0);
-      }
-      if (!mbar_wait(&acc2[db], (uint32_t)((i >> 1) & 1), DEV_TIMEOUT_ACC)) break;
-      tc_fence_after();
-      float s1 = 0.0f, s2 = 0.0f;
-#pragma unroll 1
-      for (int c = 0; c < CP / 32; c++) {
-        float v[32];
-        tmem_ld32(td2 + (uint32_t)(c * 32), v);
-#pragma unroll
-        for (int jj = 0; jj < 32; jj++) {
-          const float x = v[jj] + s_vec[HP + c * 32 + jj];
-          s1 += x;
-          s2 += x * x;
-        }
-      }
-      const float nf = (float)a.ln_n;
-      const float mean = s1 / nf;
-      const float rstd = 1.0f / sqrtf(fmaxf(s2 / nf - mean * mean, 0.0f) + a.ln_eps);
-      const float nmr = -mean * rstd;
-#pragma unroll 1
-      for (int c = half; c < CP / 32; c += 2, jcnt++) {
-        const int jb = jcnt & 1;
-        float* f32 = reinterpret_cast<float*>(wf32 + jb * 4096);
-        uint8_t* f16 = wf16 + jb * 2048;
-        float v[32];
-        tmem_ld32(td2 + (uint32_t)(c * 32), v);
-        if (c + 2 >= CP / 32) {  // this warp is done reading D2 buffer db
+          for (int u = 0; u < 4; u++) {
+            const int uu = (half * 4 + u) ^ (r & 7);
+            *reinterpret_cast<uint4*>(chunk + r * 128 + uu * 16) =
+                make_uint4(hv[4 * u], hv[4 * u + 1], hv[4 * u + 2], hv[4 * u + 3]);
+          }
+          // generic-proxy writes -> visible to the tensor core (async proxy); the D1
+          // buffer is drained
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&d2free[db]);
-        }
-        if (lane == 0 && c + 2 < CP / 32) {
-          bulk_wait_read<0>();
-          mbar_arrive_expect_tx(&wrb[jb ^ 1], 4096);
-          tma_load_2d(wf32 + (jb ^ 1) * 4096, &mapX32, &wrb[jb ^ 1], (c + 2) * 32, row0);
-        }
-        if (!mbar_wait(&wrb[jb], (jcnt >> 1) & 1, DEV_TIMEOUT_FULL)) {
-          ok = false;
-          break;
-        }
-        const int cl0 = c * 32;
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const float4 bb = *reinterpret_cast<const float4*>(s_vec + HP + cl0 + 4 * u);
-          const float4 gg = *reinterpret_cast<const float4*>(s_vec + HP + CP + cl0 + 4 * u);
-          const float4 be = *reinterpret_cast<const float4*>(s_vec + HP + 2 * CP + cl0 + 4 * u);
-          float4* slot = reinterpret_cast<float4*>(f32 + lane * 32 + ((u ^ sw128) << 2));
-          const float4 rr = *slot;
-          float4 o;
-          o.x = fmaf(fmaf(v[4 * u] + bb.x, rstd, nmr), gg.x, be.x) + rr.x;
-          o.y = fmaf(fmaf(v[4 * u + 1] + bb.y, rstd, nmr), gg.y, be.y) + rr.y;
-          o.z = fmaf(fmaf(v[4 * u + 2] + bb.z, rstd, nmr), gg.z, be.z) + rr.z;
-          o.w = fmaf(fmaf(v[4 * u + 3] + bb.w, rstd, nmr), gg.w, be.w) + rr.w;
-          *slot = o;
-          v[4 * u] = o.x;
-          v[4 * u + 1] = o.y;
-          v[4 * u + 2] = o.z;
-          v[4 * u + 3] = o.w;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          __half2 h0 = __floats2half2_rn(v[8 * u], v[8 * u + 1]);
-          __half2 h1 = __floats2half2_rn(v[8 * u + 2], v[8 * u + 3]);
-          __half2 h2 = __floats2half2_rn(v[8 * u + 4], v[8 * u + 5]);
-          __half2 h3 = __floats2half2_rn(v[8 * u + 6], v[8 * u + 7]);
-          *reinterpret_cast<uint4*>(f16 + lane * 64 + ((u ^ sw64) << 4)) =
-              make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
-                         *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&mapX32, f32, cl0, row0);
-          tma_store_2d(&mapX16o, f16, cl0, row0);
-          bulk_commit();
+          if (lane == 0) mbar_arrive(&hfull[j & 1]);
         }
       }
-      if (!ok) break;
-      // the fp16 tiles live in the hidden buffers: read out before the next epilogue 1
-      if (lane == 0) bulk_wait_read<0>();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(sfree);
+    } else {
+      // ---- epilogue 2: X <- X + LN2(D2 + b2), X16 <- fp16(X), through TMA
+      uint8_t* wf32 = stgbuf + gw * Cfg::STG;
+      uint8_t* f16 = wf32 + 2 * 4096;
+      uint64_t* wrb = rbar + 2 * gw;
+      const int sw128 = lane & 7, sw64 = (lane >> 1) & 3;  // this row's swizzle phases
+      uint32_t jcnt = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
+        const int row0 = t * 128 + q * 32;  // this warp's 32 rows as a TMA box origin
+        const int db = i & 1;
+        const uint32_t td2 = tq + (uint32_t)(Cfg::D2OFF + db * CP);
+        // the first residual tile is requested before waiting for fc2
+        if (lane == 0 && half < CP / 32) {
+          bulk_wait_read<0>();
+          mbar_arrive_expect_tx(&wrb[jcnt & 1], 4096);
+          tma_load_2d(wf32 + (jcnt & 1) * 4096, &mapX32, &wrb[jcnt & 1], half * 32, row0);
+        }
+        if (!mbar_wait(&acc2[db], (uint32_t)((i >> 1) & 1), DEV_TIMEOUT_ACC)) break;
+        tc_fence_after();
+        float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < CP / 32; c++) {
+          float v[32];
+          tmem_ld32(td2 + (uint32_t)(c * 32), v);
+#pragma unroll
+          for (int jj = 0; jj < 32; jj++) {
+            const float x = v[jj] + s_vec[HP + c * 32 + jj];
+            s1 += x;
+            s2 += x * x;
+          }
+        }
+        const float nf = (float)a.ln_n;
+        const float mean = s1 / nf;
+        const float rstd = 1.0f / sqrtf(fmaxf(s2 / nf - mean * mean, 0.0f) + a.ln_eps);
+        const float nmr = -mean * rstd;
+#pragma unroll 1
+        for (int c = half; c < CP / 32; c += 2, jcnt++) {
+          const int jb = jcnt & 1;
+          float* f32 = reinterpret_cast<float*>(wf32 + jb * 4096);
+          float v[32];
+          tmem_ld32(td2 + (uint32_t)(c * 32), v);
+          if (c + 2 >= CP / 32) {  // this warp is done reading D2 buffer db
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d2free[db]);
+          }
+          if (lane == 0) {
+            // the fp16 tile and the other fp32 buffer are free once every earlier
+            // store has read them; then the next chunk's residual goes there
+            bulk_wait_read<0>();
+            if (c + 2 < CP / 32) {
+              mbar_arrive_expect_tx(&wrb[jb ^ 1], 4096);
+              tma_load_2d(wf32 + (jb ^ 1) * 4096, &mapX32, &wrb[jb ^ 1], (c + 2) * 32, row0);
+            }
+          }
+          if (!mbar_wait(&wrb[jb], (jcnt >> 1) & 1, DEV_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          const int cl0 = c * 32;
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            const float4 bb = *reinterpret_cast<const float4*>(s_vec + HP + cl0 + 4 * u);
+            const float4 gg = *reinterpret_cast<const float4*>(s_vec + HP + CP + cl0 + 4 * u);
+            const float4 be = *reinterpret_cast<const float4*>(s_vec + HP + 2 * CP + cl0 + 4 * u);
+            float4* slot = reinterpret_cast<float4*>(f32 + lane * 32 + ((u ^ sw128) << 2));
+            const float4 rr = *slot;
+            float4 o;
+            o.x = fmaf(fmaf(v[4 * u] + bb.x, rstd, nmr), gg.x, be.x) + rr.x;
+            o.y = fmaf(fmaf(v[4 * u + 1] + bb.y, rstd, nmr), gg.y, be.y) + rr.y;
+            o.z = fmaf(fmaf(v[4 * u + 2] + bb.z, rstd, nmr), gg.z, be.z) + rr.z;
+            o.w = fmaf(fmaf(v[4 * u + 3] + bb.w, rstd, nmr), gg.w, be.w) + rr.w;
+            *slot = o;
+            v[4 * u] = o.x;
+            v[4 * u + 1] = o.y;
+            v[4 * u + 2] = o.z;
+            v[4 * u + 3] = o.w;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            __half2 h0 = __floats2half2_rn(v[8 * u], v[8 * u + 1]);
+            __half2 h1 = __floats2half2_rn(v[8 * u + 2], v[8 * u + 3]);
+            __half2 h2 = __floats2half2_rn(v[8 * u + 4], v[8 * u + 5]);
+            __half2 h3 = __floats2half2_rn(v[8 * u + 6], v[8 * u + 7]);
+            *reinterpret_cast<uint4*>(f16 + lane * 64 + ((u ^ sw64) << 4)) =
+                make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                           *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&mapX32, f32, cl0, row0);
+            tma_store_2d(&mapX16o, f16, cl0, row0);
+            bulk_commit();
+          }
+        }
+      }
+      if (lane == 0) bulk_wait<0>();
     }
-    if (lane == 0) bulk_wait<0>();
   }
 
   tc_fence_before();
@@ -425,7 +425,7 @@ cudaError_t launch_mlp(const CUtensorMap& mX, const CUtensorMap& mW1, const CUte
                        const CUtensorMap& mX32, const CUtensorMap& mX16o, const MlpArgs& a, int cp,
                        int hp, cudaStream_t st) {
   if (cp == 192 && hp == 384)
-    return launch_mlp_t<192, 384, 3>(mX, mW1, mW2, mX32, mX16o, a, st);
+    return launch_mlp_t<192, 384, 2>(mX, mW1, mW2, mX32, mX16o, a, st);
   if (cp == 64 && hp == 128)
     return launch_mlp_t<64, 128, 4>(mX, mW1, mW2, mX32, mX16o, a, st);
   return cudaErrorNotSupported;
