@@ -111,13 +111,16 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_trigger();
+  // the bias table is a weight: it loads while the previous kernel finishes
+  if (warp == CW && lane == 0) {
+    mbar_arrive_expect_tx(cbar, (uint32_t)(HPC * N * NS * 4));
+    bulk_g2s(scpb, cpb + (size_t)h0 * N * NS, HPC * N * NS * 4, cbar);
+  }
+  pdl_wait();  // QKV is complete
 
   if (warp == CW) {
     // ------------------------------------------------------------ producer warp
-    if (lane == 0) {
-      mbar_arrive_expect_tx(cbar, (uint32_t)(HPC * N * NS * 4));
-      bulk_g2s(scpb, cpb + (size_t)h0 * N * NS, HPC * N * NS * 4, cbar);
-    }
     int i = 0;
     for (int win = win0; win < nwin_total; win += wstep, i++) {
       const int b = i & 1;
@@ -309,9 +312,9 @@ cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb,
   if (G > ctas) G = ctas;
   G = (G / NG) * NG;
   if (G < NG) G = NG;
-  k_window_attention<DP, HPC><<<(unsigned)G, 128 * HPC + 32, smem, st>>>(
-      qkv, out, cpb, rows, heads, hd, ld_out, nwh, nww, hp, wp, shift, nwin_total, wh_off);
-  return cudaGetLastError();
+  return launch_pdl(k_window_attention<DP, HPC>, dim3((unsigned)G), dim3(128 * HPC + 32), smem, st,
+                    qkv, out, cpb, rows, heads, hd, ld_out, nwh, nww, hp, wp, shift, nwin_total,
+                    wh_off);
 }
 
 }  // namespace

@@ -12,7 +12,49 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+#include <cstring>
+#include <utility>
+
 namespace s2s {
+
+// ---------------------------------------------------------------- dependent launch
+// Every kernel of the library is launched with programmatic stream serialization:
+// it signals at its start that the next kernel of the stream may be scheduled
+// (pdl_trigger), and waits for the previous kernel to complete and its writes to be
+// visible (pdl_wait) after its prologue - barrier setup, TMEM allocation, tensor-map
+// prefetch, constant loads - and before touching any activation in global memory.
+// So each kernel's prologue overlaps the tail of the one before it. S2S_PDL=0 turns
+// the attribute off (plain stream order).
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("S2S_PDL");
+    return !(v && strcmp(v, "0") == 0);
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof cfg);
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Error codes recorded on the device (first error wins).
 enum : unsigned { DEV_OK = 0, DEV_TIMEOUT_FULL = 1, DEV_TIMEOUT_EMPTY = 2, DEV_TIMEOUT_ACC = 3,

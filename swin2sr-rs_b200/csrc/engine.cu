@@ -824,8 +824,14 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
   float* const X = P->X + P->own_off * Cp;       // owned rows of the residual stream
   __half* const X16 = P->X16 + P->own_off * Cp;
   float* const S = P->S + P->own_off * Cp;
+  // Halo transfers run on the side stream behind an event, so they start only once
+  // every kernel before them has completed (kernels signal their dependents early).
   auto exchange = [&](const char* name, __half* buf, int n, bool cyclic, bool zero_edges) {
-    L.comm(name, st, [&] { halo_exchange(H, P, buf, Cp, n, cyclic, zero_edges, st); });
+    ck(cudaEventRecord(H->fork, st), "fork");
+    ck(cudaStreamWaitEvent(H->side, H->fork, 0), "fork");
+    L.comm(name, H->side, [&] { halo_exchange(H, P, buf, Cp, n, cyclic, zero_edges, H->side); });
+    ck(cudaEventRecord(H->join, H->side), "join");
+    ck(cudaStreamWaitEvent(st, H->join, 0), "join");
   };
   // 1. pad + conv_first (fp32 body skip F0, fp16 operand F0h).
   if (!band) {

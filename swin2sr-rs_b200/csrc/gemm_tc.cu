@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_trigger();
+  pdl_wait();  // the previous kernel's outputs (this kernel's A operand) are complete
 
   if (warp == 0) {
     if (lane == 0) {
@@ -552,8 +554,8 @@ cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const Out
   long G = tiles < ctas ? tiles : ctas;
   G = (G / NT) * NT;
   if (G < NT) G = NT;
-  k_gemm<BN, STAGES, ACT, LN, RES, STORE><<<(unsigned)G, kThreads, smem, st>>>(mapA, mapB, om, a);
-  return cudaGetLastError();
+  return launch_pdl(k_gemm<BN, STAGES, ACT, LN, RES, STORE>, dim3((unsigned)G), dim3(kThreads), smem,
+                    st, mapA, mapB, om, a);
 }
 
 }  // namespace

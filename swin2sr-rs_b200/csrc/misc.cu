@@ -12,6 +12,8 @@ namespace {
 // src/plan.rs:116-139: [B][c][h][w] -> [B][c][hp][wp], whole-plane mirror.
 __global__ void k_pad_reflect(const float* __restrict__ x, float* __restrict__ y, int B, int c,
                               int h, int w, int hp, int wp) {
+  pdl_trigger();
+  pdl_wait();
   const size_t n = (size_t)B * c * hp * wp;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
@@ -29,6 +31,8 @@ __global__ void k_pad_reflect(const float* __restrict__ x, float* __restrict__ y
 // true edges).
 __global__ void k_pad_band(const float* __restrict__ x, float* __restrict__ y, int c, int h,
                            int w, int hp, int wp, int rows, int y0) {
+  pdl_trigger();
+  pdl_wait();
   const size_t n = (size_t)c * rows * wp;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
@@ -66,6 +70,8 @@ __global__ void __launch_bounds__(256) k_conv3_small(
   }
   for (int i = g * 32 + lane; i < kConvGroups * 8; i += 256)
     sb[i] = cbase + i < co_n ? bias[cbase + i] : 0.0f;
+  pdl_trigger();
+  pdl_wait();  // the input plane is complete
   __syncthreads();
   const int c0 = cbase + g * 8;  // this warp's first output channel
   if (c0 >= co_n) return;
@@ -134,6 +140,8 @@ __global__ void __launch_bounds__(256) k_conv3_small(
 
 // Zero the pad channels [c0, ld) of NHWC rows (so padded K lanes are finite zeros).
 __global__ void k_zero_cols_f16(__half* __restrict__ x, size_t rows, int c0, int ld) {
+  pdl_trigger();
+  pdl_wait();
   const int w = ld - c0;
   const size_t n = rows * w;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
@@ -152,6 +160,8 @@ __device__ __forceinline__ float cubic_w(float t) {
 
 __global__ void k_bicubic(const float* __restrict__ in, float* __restrict__ out, int BC, int h,
                           int w, int oh, int ow) {
+  pdl_trigger();
+  pdl_wait();
   const size_t n = (size_t)BC * oh * ow;
   const float ry = (float)h / (float)oh, rx = (float)w / (float)ow;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
@@ -186,6 +196,8 @@ __global__ void k_bicubic(const float* __restrict__ in, float* __restrict__ out,
 // Nearest x2 upsample of an NHWC fp16 plane, 16 bytes per thread.
 __global__ void k_up2_nhwc(const __half* __restrict__ in, __half* __restrict__ out, int B, int H,
                            int W, int C) {
+  pdl_trigger();
+  pdl_wait();
   const int cv = C / 8;
   const size_t n = (size_t)B * 2 * H * 2 * W * cv;
   const uint4* src = reinterpret_cast<const uint4*>(in);
@@ -211,14 +223,14 @@ inline unsigned grid_for(size_t n, int block) {
 
 cudaError_t launch_pad_reflect(const float* x, float* y, int B, int c, int h, int w, int hp,
                                int wp, cudaStream_t st) {
-  k_pad_reflect<<<grid_for((size_t)B * c * hp * wp, 256), 256, 0, st>>>(x, y, B, c, h, w, hp, wp);
-  return cudaGetLastError();
+  return launch_pdl(k_pad_reflect, dim3(grid_for((size_t)B * c * hp * wp, 256)), dim3(256), 0, st, x,
+                    y, B, c, h, w, hp, wp);
 }
 
 cudaError_t launch_pad_band(const float* x, float* y, int c, int h, int w, int hp, int wp, int rows,
                             int y0, cudaStream_t st) {
-  k_pad_band<<<grid_for((size_t)c * rows * wp, 256), 256, 0, st>>>(x, y, c, h, w, hp, wp, rows, y0);
-  return cudaGetLastError();
+  return launch_pdl(k_pad_band, dim3(grid_for((size_t)c * rows * wp, 256)), dim3(256), 0, st, x, y,
+                    c, h, w, hp, wp, rows, y0);
 }
 
 cudaError_t launch_conv3_small(const float* in, const float* wgt, const float* bias, int B, int H,
@@ -231,28 +243,27 @@ cudaError_t launch_conv3_small(const float* in, const float* wgt, const float* b
   const size_t tiles = (size_t)B * H * ((W + 31) / 32);
   // a few blocks per SM, each walking many pixel tiles: the weight staging is paid once
   const unsigned gx = (unsigned)std::min<size_t>(tiles, (size_t)148 * 3);
-  k_conv3_small<<<dim3(gx, gy), dim3(32, kConvGroups), 0, st>>>(in, wgt, bias, B, H, W, co_n, act,
-                                                                 slope, o32, ld32, o16, ld16);
-  return cudaGetLastError();
+  return launch_pdl(k_conv3_small, dim3(gx, gy), dim3(32, kConvGroups), 0, st, in, wgt, bias, B, H,
+                    W, co_n, act, slope, o32, ld32, o16, ld16);
 }
 
 cudaError_t launch_zero_cols_f16(__half* x, size_t rows, int c0, int ld, cudaStream_t st) {
   if (c0 >= ld) return cudaSuccess;
-  k_zero_cols_f16<<<grid_for(rows * (ld - c0), 256), 256, 0, st>>>(x, rows, c0, ld);
-  return cudaGetLastError();
+  return launch_pdl(k_zero_cols_f16, dim3(grid_for(rows * (ld - c0), 256)), dim3(256), 0, st, x,
+                    rows, c0, ld);
 }
 
 cudaError_t launch_bicubic(const float* in, float* out, int BC, int h, int w, int oh, int ow,
                            cudaStream_t st) {
-  k_bicubic<<<grid_for((size_t)BC * oh * ow, 256), 256, 0, st>>>(in, out, BC, h, w, oh, ow);
-  return cudaGetLastError();
+  return launch_pdl(k_bicubic, dim3(grid_for((size_t)BC * oh * ow, 256)), dim3(256), 0, st, in, out,
+                    BC, h, w, oh, ow);
 }
 
 cudaError_t launch_up2_nhwc(const __half* in, __half* out, int B, int H, int W, int C,
                             cudaStream_t st) {
   if (C % 8) return cudaErrorInvalidValue;
-  k_up2_nhwc<<<grid_for((size_t)B * 4 * H * W * (C / 8), 256), 256, 0, st>>>(in, out, B, H, W, C);
-  return cudaGetLastError();
+  return launch_pdl(k_up2_nhwc, dim3(grid_for((size_t)B * 4 * H * W * (C / 8), 256)), dim3(256), 0,
+                    st, in, out, B, H, W, C);
 }
 
 }  // namespace s2s

@@ -105,6 +105,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  pdl_trigger();
+  pdl_wait();  // the previous kernel's outputs (X, X16) are complete
 
   if (warp == 0) {
     if (lane == 0) {
@@ -415,8 +417,8 @@ cudaError_t launch_mlp_t(const CUtensorMap& mX, const CUtensorMap& mW1, const CU
   }
   const int tiles = (a.M + 127) / 128;
   const int G = tiles < ctas ? tiles : ctas;
-  k_mlp<CP, HP, STAGES><<<G, kMlpThreads, Cfg::SMEM, st>>>(mX, mW1, mW2, mX32, mX16o, a);
-  return cudaGetLastError();
+  return launch_pdl(k_mlp<CP, HP, STAGES>, dim3(G), dim3(kMlpThreads), Cfg::SMEM, st, mX, mW1, mW2,
+                    mX32, mX16o, a);
 }
 
 }  // namespace
