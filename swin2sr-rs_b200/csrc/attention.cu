@@ -4,8 +4,9 @@
 // Persistent CTAs, each owning a group of HPC heads and walking windows: one producer
 // warp and 4*HPC compute warps, one (head, 16-query-row block) task per compute warp
 // and window, with no block-wide barrier in the window loop. The group's position-bias
-// table ([HPC][64][72] fp32, rows padded for conflict-free reads) is brought into
-// shared memory once; the producer gathers each window's q/k/v rows of those heads by
+// table ([HPC][64][64] fp32, columns XOR-swizzled by row % 8 for conflict-free reads)
+// is brought into shared memory once; the producer gathers each window's q/k/v rows of
+// those heads by
 // bulk copies into one of two buffers (full/empty mbarriers), so the next window's
 // copies overlap this window's math. The QKV projection's epilogue has already
 // L2-normalised q and k and scaled q by exp(min(logit_scale, ln 100)) * log2 e, and the
@@ -83,7 +84,7 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     const int* __restrict__ rows, int heads, int hd, int ld_out,
     int nwh, int nww, int hp, int wp, int shift, int nwin_total, int wh_off) {
   constexpr int N = 64;
-  constexpr int NS = N + 8;                    // padded bias row (floats)
+  constexpr int NS = N;                        // bias row (floats), XOR-swizzled by row % 8
   constexpr int SEG = HPC * 3 * DP;            // halves of this CTA's heads per token row
   constexpr int SSTRIDE = SEG + 8;             // padded smem row: odd number of 16 B units
   constexpr int CW = 4 * HPC;                  // compute warps
@@ -207,8 +208,9 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       const int k = 8 * j + 2 * t4;
-      const float2 b0 = *reinterpret_cast<const float2*>(cp0 + k);
-      const float2 b1 = *reinterpret_cast<const float2*>(cp1 + k);
+      const int ks = k ^ (g << 2);  // both query rows have row % 8 == g
+      const float2 b0 = *reinterpret_cast<const float2*>(cp0 + ks);
+      const float2 b1 = *reinterpret_cast<const float2*>(cp1 + ks);
       float s00 = sacc[j][0] + b0.x;
       float s01 = sacc[j][1] + b0.y;
       float s10 = sacc[j][2] + b1.x;
@@ -292,7 +294,7 @@ cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb,
                           const int* rows, int nwin_total, int heads, int hd, int ld_out, int nwh,
                           int nww, int hp, int wp, int shift, int wh_off, cudaStream_t st) {
   constexpr int SEG = HPC * 3 * DP;
-  const size_t smem = (size_t)HPC * 64 * 72 * 4 + (size_t)2 * 64 * (SEG + 8) * 2 + 5 * 8 + 16;
+  const size_t smem = (size_t)HPC * 64 * 64 * 4 + (size_t)2 * 64 * (SEG + 8) * 2 + 5 * 8 + 16;
   static int ctas = 0;  // resident CTAs per device
   if (ctas == 0) {
     cudaError_t err = cudaFuncSetAttribute(k_window_attention<DP, HPC>,
@@ -323,7 +325,10 @@ cudaError_t launch_window_attention(const __half* qkv, __half* out, const float*
                                     const int* rows, int nwin_total,
                                     int heads, int hd, int dp, int ld_out, int nwh, int nww,
                                     int hp, int wp, int shift, int wh_off, cudaStream_t st) {
-  const bool pair = heads % 2 == 0;
+  // one head per CTA: the smallest CTA (about 43 KB of shared memory), so five fit on
+  // an SM and their window streams hide each other's latency (two heads per CTA, two
+  // CTAs per SM, measured 11 % slower)
+  const bool pair = false;
   if (dp == 32 && pair)
     return launch_attn_t<32, 2>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
                                 nww, hp, wp, shift, wh_off, st);

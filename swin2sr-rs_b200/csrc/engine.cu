@@ -328,17 +328,18 @@ void build_weights(s2s_handle* H, const TensorTable& T) {
       bl.n1b = upload(H, padded(T.get(p + "norm1.bias", C), C, Cp));
       bl.n2g = upload(H, padded(T.get(p + "norm2.weight", C), C, Cp));
       bl.n2b = upload(H, padded(T.get(p + "norm2.bias", C), C, Cp));
-      // cpb_pre [N*N][heads] -> [heads][N][N + 8] (rows padded so that the attention
-      // kernel's shared-memory reads are free of bank conflicts); logit scale ->
-      // exp(min(ls, ln 100)). Both times log2 e: the attention kernel's softmax is exp2.
+      // cpb_pre [N*N][heads] -> [heads][N][N], key column k of query row q stored at
+      // k ^ ((q % 8) * 4) (the attention kernel's shared-memory reads are then free of
+      // bank conflicts); logit scale -> exp(min(ls, ln 100)). Both times log2 e: the
+      // attention kernel's softmax is exp2.
       const float kLog2e = 1.4426950408889634f;
       const float* cpb = T.get(p + "attn.cpb_pre", (int64_t)n * n * heads);
-      const int ns = n + 8;
-      std::vector<float> cpbt((size_t)heads * n * ns, 0.0f);
+      std::vector<float> cpbt((size_t)heads * n * n, 0.0f);
       for (int q = 0; q < n; q++)
         for (int k = 0; k < n; k++)
           for (int h = 0; h < heads; h++)
-            cpbt[((size_t)h * n + q) * ns + k] = cpb[((size_t)q * n + k) * heads + h] * kLog2e;
+            cpbt[((size_t)h * n + q) * n + (k ^ ((q & 7) << 2))] =
+                cpb[((size_t)q * n + k) * heads + h] * kLog2e;
       bl.cpb = upload(H, cpbt);
       const float* ls = T.get(p + "attn.logit_scale", heads);
       std::vector<float> lse(heads);
