@@ -4,6 +4,10 @@
                   ``aux()``.
 * ``Pre``       - the window check and the mean adjustment (src/backend.rs:53-87).
 * ``run_tiled`` - the tile loop that calls ``forward`` (src/backend.rs:92-164).
+* ``crop_side``, ``auto_tile`` - the tile the memory budget allows
+                  (src/backend.rs:168-259), from the library's exact workspace size.
+* ``run_with_fallback`` - halve the tile and retry when the device runs out of
+                  memory (src/main.rs:579-662).
 * ``Gpu``       - the B200 backend: ``forward`` goes through the C ABI
                   (include/s2s.h) into the sm_100a kernels. There is no CPU fallback.
 """
@@ -65,6 +69,10 @@ class Gpu(Backend):
     def aux(self):
         return self._aux
 
+    def workspace_bytes(self, h: int, w: int) -> int:
+        """Device bytes a forward of one h x w image allocates (s2s_workspace_bytes)."""
+        return self.handle.workspace_bytes(1, h, w)
+
     def close(self):
         self.handle.close()
 
@@ -97,3 +105,68 @@ def run_tiled(wt, backend: Backend, img: np.ndarray, tile: int, pad: int) -> np.
             tx += tile
         ty += tile
     return out
+
+
+def crop_side(h: int, w: int, tile: int, pad: int, win: int) -> int:
+    """src/backend.rs:249-259: the padded plane, in pixels a side, that a crop of
+    `tile` pixels plus `pad` of context runs on (tile 0 = the whole image)."""
+    if tile == 0:
+        th, tw = h, w
+    else:
+        t = max(tile // win, 1) * win
+        p = max(-(-pad // win), 1) * win
+        th, tw = min(t + 2 * p, h), min(t + 2 * p, w)
+    plane = lambda n: (n // win + 1) * win  # noqa: E731
+    return max(plane(th), plane(tw))
+
+
+def auto_tile(wt, backend, budget: int, h: int, w: int, pad: int) -> int:
+    """src/backend.rs:168-187: 0 when the whole image fits `budget` bytes of
+    activations, else the largest window-multiple tile (from 1024, halving) whose
+    crop fits. The size of a crop comes from the backend's own exact workspace
+    figure (s2s_workspace_bytes) rather than a per-pixel estimate; the device
+    kernels have no launch-size ceiling to check besides it."""
+    win = wt.window
+    pad = max(-(-pad // win), 1) * win
+    whole = crop_side(h, w, 0, pad, win)
+    # crop_side reports the padded plane; the workspace is asked for the crop itself
+    if backend.workspace_bytes(whole - win, whole - win) <= budget:
+        return 0
+    t = (max(1024, win) // win) * win
+    while True:
+        side = crop_side(h, w, t, pad, win)
+        if backend.workspace_bytes(side - win, side - win) <= budget or t == win:
+            return t
+        t = max(t // 2 // win, 1) * win
+
+
+def is_out_of_memory(err: Exception) -> bool:
+    """src/main.rs:660-662: the one failure a smaller tile can fix."""
+    msg = str(err)
+    return "OUT_OF_MEMORY" in msg or "out of memory" in msg
+
+
+def run_with_fallback(wt, backend: Backend, img: np.ndarray, tile: int, pad: int,
+                      note=None):
+    """src/main.rs:579-657: run_tiled, halving the tile on out-of-memory (a failed
+    whole-image pass falls back to half the image), down to one window.
+    Returns (image, the tile that ran). `note` receives each retry's message."""
+    for _ in range(64):
+        try:
+            return run_tiled(wt, backend, img, tile, pad), tile
+        except Exception as e:  # noqa: BLE001 - only out-of-memory is retried
+            if not (is_out_of_memory(e) and (tile > wt.window or tile == 0)):
+                raise
+            _, ih, iw = img.shape
+            if tile == 0:
+                nxt = max(max(ih, iw) // 2 // wt.window, 1) * wt.window
+            else:
+                nxt = max(tile // 2 // wt.window, 1) * wt.window
+            shrinking = nxt != 0 if tile == 0 else nxt < tile
+            if not shrinking or nxt == 0:
+                raise RuntimeError(f"{e}\n(a {wt.window}-pixel tile is the smallest this engine "
+                                   f"will run, and it did not fit either)") from e
+            if note:
+                note(f"{e} - retrying with a {nxt}x{nxt} tile")
+            tile = nxt
+    raise RuntimeError(f"gave up after 64 tile reductions at tile {tile}")
