@@ -181,15 +181,22 @@ class Handle:
         self._check(self.L.s2s_aux_dims(self.h, h, w, ctypes.byref(ah), ctypes.byref(aw)))
         return ah.value, aw.value
 
-    def forward_batch(self, x: np.ndarray):
-        """[B][3][h][w] mean-adjusted -> ([B][3][h*s][w*s], aux [B][3][hp][wp] or None)."""
+    def forward_batch(self, x: np.ndarray, out: np.ndarray | None = None,
+                      aux: np.ndarray | None = None):
+        """[B][3][h][w] mean-adjusted -> ([B][3][h*s][w*s], aux [B][3][hp][wp] or None).
+        `out` / `aux` may be caller buffers (page-locked ones are written directly)."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         B, _, h, w = x.shape
         s, win = self.wt.scale, self.wt.window
-        out = np.empty((B, 3, h * s, w * s), np.float32)
-        aux = None
+        if out is None:
+            out = np.empty((B, 3, h * s, w * s), np.float32)
+        assert out.shape == (B, 3, h * s, w * s) and out.dtype == np.float32
+        assert out.flags.c_contiguous
         if self.wt.upsampler == "pixelshuffle_aux":
-            aux = np.empty((B, 3, (h // win + 1) * win, (w // win + 1) * win), np.float32)
+            if aux is None:
+                aux = np.empty((B, 3, (h // win + 1) * win, (w // win + 1) * win), np.float32)
+        else:
+            aux = None
         self._check(self.L.s2s_forward_batch(self.h, B, h, w, _fp(x), _fp(out),
                                              _fp(aux) if aux is not None else None))
         return out, aux

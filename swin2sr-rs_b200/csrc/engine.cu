@@ -1257,6 +1257,19 @@ int guarded(s2s_handle* H, F&& f) {
   }
 }
 
+// The device address of a page-locked (pinned, mapped) host buffer, or null for
+// pageable memory: the final kernels then store the output straight into the
+// caller's buffer and no separate download runs.
+float* pinned_alias(float* host) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, host) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (at.type != cudaMemoryTypeHost || !at.devicePointer) return nullptr;
+  return static_cast<float*>(at.devicePointer);
+}
+
 void ensure_staging(s2s_handle* H, float** p, size_t* have, size_t n) {
   if (*have >= n) return;
   if (*p) cudaFree(*p);
@@ -1393,13 +1406,17 @@ int s2s_forward_batch(s2s_handle* H, int batch, int height, int width, const flo
     const size_t naux = (size_t)batch * 3 * (height / win + 1) * win * (width / win + 1) * win;
     const bool has_aux = H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX;
     ensure_staging(H, &H->h_in, &H->h_in_n, nin);
-    ensure_staging(H, &H->h_out, &H->h_out_n, nout);
-    if (has_aux) ensure_staging(H, &H->h_aux, &H->h_aux_n, naux);
+    // pinned caller buffers are written by the final kernels directly
+    float* d_out = pinned_alias(out);
+    float* d_aux = has_aux && aux ? pinned_alias(aux) : nullptr;
+    if (!d_out) ensure_staging(H, &H->h_out, &H->h_out_n, nout);
+    if (has_aux && !d_aux) ensure_staging(H, &H->h_aux, &H->h_aux_n, naux);
     ck(cudaMemcpyAsync(H->h_in, in, nin * 4, cudaMemcpyHostToDevice, H->stream), "upload");
-    run_forward(H, batch, height, width, H->h_in, H->h_out, has_aux ? H->h_aux : nullptr,
-                   H->stream);
-    ck(cudaMemcpyAsync(out, H->h_out, nout * 4, cudaMemcpyDeviceToHost, H->stream), "download");
-    if (has_aux && aux)
+    run_forward(H, batch, height, width, H->h_in, d_out ? d_out : H->h_out,
+                has_aux ? (d_aux ? d_aux : H->h_aux) : nullptr, H->stream);
+    if (!d_out)
+      ck(cudaMemcpyAsync(out, H->h_out, nout * 4, cudaMemcpyDeviceToHost, H->stream), "download");
+    if (has_aux && aux && !d_aux)
       ck(cudaMemcpyAsync(aux, H->h_aux, naux * 4, cudaMemcpyDeviceToHost, H->stream), "download");
     ck(cudaStreamSynchronize(H->stream), "forward");
     check_device_error(H);
@@ -1635,10 +1652,11 @@ int s2s_forward_band_host(s2s_handle* H, int height, int width, const float* in,
     const size_t nin = (size_t)3 * height * width;
     const size_t nout = (size_t)3 * (r1 - r0) * s * width * s;
     ensure_staging(H, &H->h_in, &H->h_in_n, nin);
-    ensure_staging(H, &H->h_out, &H->h_out_n, std::max(nout, (size_t)1));
+    float* d_out = pinned_alias(out);  // pinned caller buffers are written directly
+    if (!d_out) ensure_staging(H, &H->h_out, &H->h_out_n, std::max(nout, (size_t)1));
     ck(cudaMemcpyAsync(H->h_in, in, nin * 4, cudaMemcpyHostToDevice, H->stream), "upload");
-    run_forward(H, 1, height, width, H->h_in, H->h_out, nullptr, H->stream);
-    if (nout)
+    run_forward(H, 1, height, width, H->h_in, d_out ? d_out : H->h_out, nullptr, H->stream);
+    if (nout && !d_out)
       ck(cudaMemcpyAsync(out, H->h_out, nout * 4, cudaMemcpyDeviceToHost, H->stream), "download");
     ck(cudaStreamSynchronize(H->stream), "forward");
     check_device_error(H);

@@ -56,7 +56,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accf = empty + STAGES;   // [2] accumulator ready
   uint64_t* acce = accf + 2;         // [2] accumulator drained
   uint64_t* fin = acce + 2;          // all MMAs of this CTA retired
-  uint64_t* rbar = fin + 1;          // [kEpiWarps][2] residual tile landed
+  uint64_t* bfull = fin + 1;         // resident B (all K-slices) landed
+  uint64_t* rbar = bfull + 1;        // [kEpiWarps][2] residual tile landed
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rbar + 2 * kEpiWarps);
 
   const int warp = threadIdx.x >> 5;
@@ -98,6 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acce[b], kEpiWarps);
     }
     mbar_init(fin, 1);
+    mbar_init(bfull, 1);
     for (int k = 0; k < 2 * kEpiWarps; k++) mbar_init(&rbar[k], 1);
     fence_barrier_init();
   }
@@ -112,9 +114,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_trigger();
   pdl_wait();  // the previous kernel's outputs (this kernel's A operand) are complete
 
+  // When all of this CTA's B (its N tile over the whole K) fits the ring's B slots -
+  // a GEMM with K <= 64 * STAGES - it is loaded once and stays resident; the ring then
+  // streams A only.
+  const bool bres = !a.conv && num_k <= STAGES;
+
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- producer
+      if (bres) {
+        mbar_arrive_expect_tx(bfull, (uint32_t)(num_k * B_BYTES));
+        for (int k = 0; k < num_k; k++) tma_load_2d(sB + k * B_BYTES, &mapB, bfull, k * 64, n0);
+      }
       uint32_t kit = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += G) {
@@ -127,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+          mbar_arrive_expect_tx(&full[s], bres ? A_BYTES : A_BYTES + B_BYTES);
           if (!a.conv) {
             tma_load_2d(sA + s * A_BYTES, &mapA, &full[s], k * 64, m0);
           } else {
@@ -136,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_4d(sA + s * A_BYTES, &mapA, &full[s], cc * 64, x0 + kx - 1, y0 + ky - 1,
                         bimg);
           }
-          tma_load_2d(sB + s * B_BYTES, &mapB, &full[s], k * 64, n0);
+          if (!bres) tma_load_2d(sB + s * B_BYTES, &mapB, &full[s], k * 64, n0);
         }
       }
     }
@@ -145,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc = idesc_f16_f32(128, BN);
       uint32_t kit = 0;
-      bool ok = true;
+      bool ok = !bres || mbar_wait(bfull, 0, DEV_TIMEOUT_FULL);
       int i = 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += G, i++) {
         const int b = i & 1;
@@ -160,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint64_t ad = sw128_desc(smem_u32(sA + s * A_BYTES));
-          const uint64_t bd = sw128_desc(smem_u32(sB + s * B_BYTES));
+          const uint64_t bd = sw128_desc(smem_u32(sB + (bres ? k : s) * B_BYTES));
 #pragma unroll
           for (int kk = 0; kk < 4; kk++) {
             tc_mma_f16(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
@@ -533,7 +544,7 @@ template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE>
 cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const OutMaps& om,
                      const GemmArgs& a, cudaStream_t st) {
   const size_t smem = 1024 + (size_t)STAGES * (128 * 128 + BN * 128) + kEpiWarps * kWarpBuf +
-                      3 * BN * 4 + kEpiWarps * 32 * 4 * 4 + (2 * STAGES + 5 + 2 * kEpiWarps) * 8 +
+                      3 * BN * 4 + kEpiWarps * 32 * 4 * 4 + (2 * STAGES + 6 + 2 * kEpiWarps) * 8 +
                       16;
   static int ctas = 0;  // resident CTAs per device (SMs x CTAs per SM), one process per GPU
   if (ctas == 0) {

@@ -182,3 +182,32 @@ def test_classical_x4_full_size_matches_oracle():
     out = gpu.forward(240, 320, x)
     ref, _ = oracle().forward(wt, 240, 320, x)
     check(out, ref, "classical-x4 240x320")
+
+
+@pytest.mark.parametrize("task", ["classical_sr", "compressed_sr"])
+def test_pinned_output_buffers_are_written_directly(task):
+    """A page-locked output (and aux) buffer is the final kernels' destination (no
+    staging copy); the result equals the one through a pageable buffer."""
+    import torch
+    capi = importlib.import_module("swin2sr_b200.capi")
+    P = pkg()
+    wt = P.weights.Weights.seeded(task, 0, True)
+    H = capi.Handle(wt)
+    try:
+        x = adjust(wt, np.random.default_rng(13).random((2, 3, 27, 35), dtype=np.float32))
+        ref, ref_aux = H.forward_batch(x)
+        s = wt.scale
+        pin = torch.empty((2, 3, 27 * s, 35 * s), dtype=torch.float32).pin_memory().numpy()
+        pin[...] = np.nan
+        pin_aux = None
+        if ref_aux is not None:
+            pin_aux = torch.empty(ref_aux.shape, dtype=torch.float32).pin_memory().numpy()
+            pin_aux[...] = np.nan
+        for _ in range(3):          # eager, captured, replayed
+            out, aux = H.forward_batch(x, out=pin, aux=pin_aux)
+            assert out is pin
+            assert np.array_equal(out, ref)
+            if ref_aux is not None:
+                assert np.array_equal(aux, ref_aux)
+    finally:
+        H.close()
