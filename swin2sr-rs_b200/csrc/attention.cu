@@ -82,7 +82,7 @@ template <int DP, int HPC>
 __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     const __half* __restrict__ qkv, __half* __restrict__ out, const float* __restrict__ cpb,
     const int* __restrict__ rows, int heads, int hd, int ld_out,
-    int nwh, int nww, int hp, int wp, int shift, int nwin_total, int wh_off, int wh_step) {
+    int nwh, int nww, int hp, int wp, int shift, int nwin_total, int wh_off) {
   constexpr int N = 64;
   constexpr int NS = N;                        // bias row (floats), XOR-swizzled by row % 8
   constexpr int SEG = HPC * 3 * DP;            // halves of this CTA's heads per token row
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
     const uint32_t sbase = sbase0 + (uint32_t)(b * N * SSTRIDE * 2);
     const int wi = win % nw;
     // window row on the (global) hp x wp plane the shift mask is defined on
-    int wh = (wi / nww) * wh_step + wh_off;
+    int wh = wi / nww + wh_off;
     if (wh < 0) wh += nwh_g;
     const int ww = wi % nww;
     // Only the last window row and column of a shifted block mix roll regions.
@@ -292,8 +292,7 @@ __global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
 template <int DP, int HPC>
 cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb,
                           const int* rows, int nwin_total, int heads, int hd, int ld_out, int nwh,
-                          int nww, int hp, int wp, int shift, int wh_off, int wh_step,
-                          cudaStream_t st) {
+                          int nww, int hp, int wp, int shift, int wh_off, cudaStream_t st) {
   constexpr int SEG = HPC * 3 * DP;
   const size_t smem = (size_t)HPC * 64 * 64 * 4 + (size_t)2 * 64 * (SEG + 8) * 2 + 5 * 8 + 16;
   static int ctas = 0;  // resident CTAs per device
@@ -317,7 +316,7 @@ cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb,
   if (G < NG) G = NG;
   return launch_pdl(k_window_attention<DP, HPC>, dim3((unsigned)G), dim3(128 * HPC + 32), smem, st,
                     qkv, out, cpb, rows, heads, hd, ld_out, nwh, nww, hp, wp, shift, nwin_total,
-                    wh_off, wh_step);
+                    wh_off);
 }
 
 }  // namespace
@@ -325,24 +324,23 @@ cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb,
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
                                     const int* rows, int nwin_total,
                                     int heads, int hd, int dp, int ld_out, int nwh, int nww,
-                                    int hp, int wp, int shift, int wh_off, int wh_step,
-                                    cudaStream_t st) {
+                                    int hp, int wp, int shift, int wh_off, cudaStream_t st) {
   // one head per CTA: the smallest CTA (about 43 KB of shared memory), so five fit on
   // an SM and their window streams hide each other's latency (two heads per CTA, two
   // CTAs per SM, measured 11 % slower)
   const bool pair = false;
   if (dp == 32 && pair)
     return launch_attn_t<32, 2>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, wh_off, wh_step, st);
+                                nww, hp, wp, shift, wh_off, st);
   if (dp == 32)
     return launch_attn_t<32, 1>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, wh_off, wh_step, st);
+                                nww, hp, wp, shift, wh_off, st);
   if (dp == 16 && pair)
     return launch_attn_t<16, 2>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, wh_off, wh_step, st);
+                                nww, hp, wp, shift, wh_off, st);
   if (dp == 16)
     return launch_attn_t<16, 1>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, wh_off, wh_step, st);
+                                nww, hp, wp, shift, wh_off, st);
   return cudaErrorInvalidValue;
 }
 

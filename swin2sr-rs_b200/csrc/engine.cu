@@ -35,8 +35,7 @@ namespace s2s {
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
                                     const int* rows, int nwin_total,
                                     int heads, int hd, int dp, int ld_out, int nwh, int nww,
-                                    int hp, int wp, int shift, int wh_off, int wh_step,
-                                    cudaStream_t st);
+                                    int hp, int wp, int shift, int wh_off, cudaStream_t st);
 cudaError_t launch_pad_reflect(const float* x, float* y, int B, int c, int h, int w, int hp,
                                int wp, cudaStream_t st);
 cudaError_t launch_pad_band(const float* x, float* y, int c, int h, int w, int hp, int wp, int rows,
@@ -107,11 +106,14 @@ struct Plan {
   int own_rows = 0;     // owned plane rows
   size_t own_off = 0;   // tokens before the first owned row
   int M_own = 0;        // owned tokens (the per-token GEMMs' M)
+  size_t sh_off = 0;    // tokens before the first row the shifted windows cover
+  int M_sh = 0;         // tokens the shifted blocks' QKV covers
   int nwin[2] = {0, 0}, nwh_l[2] = {0, 0}, wh_off[2] = {0, 0};  // attention, shift 0 / win/2
-  int nb = 0, w0 = 0;   // band: owned window rows, first owned global window row
   int conv_row0 = 0, conv_H = 0, conv_y0 = 0, conv_y1 = 0;  // 3x3 conv: map rows, output rows
   int head_row0 = 0, head_rows = 0;  // the plane the upsampling head runs on
   int crop_y0 = 0, crop_rows = 0;    // output LR rows: head plane rows [crop_y0, +crop_rows)
+  CUtensorMap mX16s;                 // QKV operand of the shifted blocks
+  CUtensorMap mX16t, mX16b;          // band: the 4 halo rows above / below the owned rows
   // The forward captured as a CUDA graph for one set of I/O pointers: made on the
   // second forward with the same pointers, replayed from the third on.
   cudaGraphExec_t gexec = nullptr;
@@ -469,7 +471,7 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
   if (!band) {
     P->hp = P->ghp;
     P->own_rows = P->hp;
-    P->M_own = B * P->hp * wp;
+    P->M_own = P->M_sh = B * P->hp * wp;
     for (int i = 0; i < 2; i++) {
       P->nwh_l[i] = P->hp / 8;
       P->nwin[i] = B * P->nwh_l[i] * nww;
@@ -496,8 +498,8 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
     P->own_off = (size_t)P->halo * wp;
     P->M_own = P->own_rows * wp;
     // shifted windows cover global rows [R0 - 4, R1 + 4): local [4, hp - 4)
-    P->nb = nb;
-    P->w0 = w0;
+    P->sh_off = (size_t)(P->halo - 4) * wp;
+    P->M_sh = (P->own_rows + 8) * wp;
     P->nwh_l[0] = nb;
     P->nwin[0] = nb * nww;
     P->wh_off[0] = w0;
@@ -518,7 +520,6 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
     P->crop_rows = std::max(0, std::min(P->R1, h) - P->R0);
   }
   const int hp = P->hp;
-  const int nb_ = band ? P->nb : 0;
   const size_t T = (size_t)B * hp * wp;
   P->T = T;
   const int Cp = H->Cp, s = H->cfg.scale;
@@ -559,29 +560,17 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
         }
       }
     } else {
-      // unshifted: the owned window rows; shifted: the window rows j = 0 .. nb
-      // straddling them (local rows [4 + 8j, 12 + 8j), columns rolled by 4 with the
-      // plane's wrap), ordered interior rows 1 .. nb-1 first, then the two edge rows
-      // 0 and nb, which read the neighbours' rows
+      // unshifted: the owned window rows; shifted: window rows straddling them,
+      // local rows [4 + 8j, 12 + 8j), columns rolled by 4 with the plane's wrap
       for (int sh = 0; sh < 2; sh++) {
         rt[sh].resize((size_t)P->nwin[sh] * 64);
-        std::vector<int> order;
-        if (!sh) {
-          for (int j = 0; j < nb_; j++) order.push_back(j);
-        } else {
-          for (int j = 1; j < nb_; j++) order.push_back(j);
-          order.push_back(0);
-          order.push_back(nb_);
-        }
         const int y00 = sh ? P->halo - 4 : P->halo, x0 = sh ? win / 2 : 0;
-        for (int wi = 0; wi < P->nwin[sh]; wi++) {
-          const int j = order[wi / nww];
+        for (int wi = 0; wi < P->nwin[sh]; wi++)
           for (int t = 0; t < 64; t++) {
-            const int y = y00 + j * 8 + t / 8;
+            const int y = y00 + (wi / nww) * 8 + t / 8;
             const int x = ((wi % nww) * 8 + t % 8 + x0) % wp;
             rt[sh][(size_t)wi * 64 + t] = y * wp + x;
           }
-        }
       }
     }
     for (int i = 0; i < 2; i++)
@@ -592,6 +581,12 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
   bool ok = true;
   ok &= make_map_rows(&P->mF0h, P->F0h + P->own_off * Cp, P->M_own, Cp, 128);
   ok &= make_map_rows(&P->mX16, P->X16 + P->own_off * Cp, P->M_own, Cp, 128);
+  ok &= make_map_rows(&P->mX16s, P->X16 + P->sh_off * Cp, P->M_sh, Cp, 128);
+  if (band) {
+    ok &= make_map_rows(&P->mX16t, P->X16 + P->sh_off * Cp, (uint64_t)4 * wp, Cp, 128);
+    ok &= make_map_rows(&P->mX16b, P->X16 + (P->own_off + P->M_own) * Cp, (uint64_t)4 * wp, Cp,
+                        128);
+  }
   ok &= make_map_rows(&P->mAO, P->AO + P->own_off * Cp, P->M_own, Cp, 128);
   if (P->H16) ok &= make_map_rows(&P->mH16, P->H16 + P->own_off * H->HIDp, P->M_own, H->HIDp, 128);
   {
@@ -886,30 +881,27 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         GemmArgs a = gemm_args(rows, H->NQ, Cp, e);
         L.run("gemm_qkv", [&] { return launch_gemm(mA, bl.qkv.map, out_maps(P, a), a, bl.qkv.BN, st); });
       };
-      qkv(P->mX16, P->own_off, M);
-      auto attention = [&](const int* rows, int nwin, int nwh, int wh_off, int wh_step) {
-        L.run("window_attention", [&] {
-          return launch_window_attention(P->QKV, P->AO, bl.cpb, rows, nwin, H->heads, H->hd,
-                                         H->DP, Cp, nwh, wp / 8, P->ghp, wp, sh, wh_off, wh_step,
-                                         st);
-        });
-      };
       if (band && sh) {
-        // The shifted windows reach 4 rows into each neighbouring band (cyclically):
-        // the neighbours' finished QKV rows travel on the side stream while the
-        // interior window rows run; the two edge window rows follow their arrival.
-        const int nww = wp / 8;
+        // The shifted windows reach 4 rows into each neighbouring band (cyclically).
+        // Those rows travel on the side stream while the owned rows' QKV runs; the
+        // halo rows' QKV follows their arrival.
         ck(cudaEventRecord(H->fork, st), "fork");
         ck(cudaStreamWaitEvent(H->side, H->fork, 0), "fork");
         L.comm("halo_shift", H->side,
-               [&] { halo_exchange(H, P, P->QKV, H->NQ, 4, true, false, H->side); });
+               [&] { halo_exchange(H, P, P->X16, Cp, 4, true, false, H->side); });
         ck(cudaEventRecord(H->join, H->side), "join");
-        if (P->nb > 1) attention(P->rows[1], (P->nb - 1) * nww, P->nb - 1, P->w0, 1);
+        qkv(P->mX16, P->own_off, M);
         ck(cudaStreamWaitEvent(st, H->join, 0), "join");
-        attention(P->rows[1] + (size_t)(P->nb - 1) * nww * 64, 2 * nww, 2, P->w0 - 1, P->nb);
+        qkv(P->mX16t, P->sh_off, 4 * wp);
+        qkv(P->mX16b, P->own_off + M, 4 * wp);
       } else {
-        attention(P->rows[k], P->nwin[k], P->nwh_l[k], P->wh_off[k], 1);
+        qkv(P->mX16, P->own_off, M);
       }
+      L.run("window_attention", [&] {
+        return launch_window_attention(P->QKV, P->AO, bl.cpb, P->rows[k], P->nwin[k],
+                                       H->heads, H->hd, H->DP, Cp, P->nwh_l[k], wp / 8, P->ghp,
+                                       wp, sh, P->wh_off[k], st);
+      });
       {  // proj + norm1 + residual, in place
         Epi e = epi0();
         e.bias = bl.proj.b;
