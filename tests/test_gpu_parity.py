@@ -211,3 +211,31 @@ def test_pinned_output_buffers_are_written_directly(task):
                 assert np.array_equal(aux, ref_aux)
     finally:
         H.close()
+
+
+@pytest.mark.parametrize("task", ["classical_sr", "lightweight_sr"])
+def test_unfused_mlp_path_matches_the_fused_kernel(task, monkeypatch):
+    """S2S_UNFUSED_MLP (read at create) runs the MLP as two GEMMs with the hidden in
+    HBM: the same fp16 hidden, the same fc2 K order, so the output must agree with
+    the fused kernel to rounding."""
+    capi = importlib.import_module("swin2sr_b200.capi")
+    P = pkg()
+    wt = P.weights.Weights.seeded(task, 0, True)
+    x = adjust(wt, np.random.default_rng(17).random((1, 3, 33, 41), dtype=np.float32))
+    H = capi.Handle(wt)
+    try:
+        fused = H.forward_batch(x)[0]
+    finally:
+        H.close()
+    monkeypatch.setenv("S2S_UNFUSED_MLP", "1")
+    H = capi.Handle(wt)
+    try:
+        unfused = H.forward_batch(x)[0]
+        H.profile(True)
+        H.forward_batch(x)
+        assert "gemm_fc1" in H.profile_report() and "mlp_fused" not in H.profile_report()
+    finally:
+        H.close()
+    err = float(np.abs(fused - unfused).max())
+    print(f"{task}: fused vs unfused MLP max-abs {err:.3e}")
+    assert err <= 1e-4
