@@ -233,7 +233,8 @@ def test_unfused_mlp_path_matches_the_fused_kernel(task, monkeypatch):
         unfused = H.forward_batch(x)[0]
         H.profile(True)
         H.forward_batch(x)
-        assert "gemm_fc1" in H.profile_report() and "mlp_fused" not in H.profile_report()
+        rep = H.profile_report()
+        assert "gemm_fc1" in rep and "mlp_fused" not in rep
     finally:
         H.close()
     err = float(np.abs(fused - unfused).max())
