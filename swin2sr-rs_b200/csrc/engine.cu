@@ -10,8 +10,10 @@
 //   conv planes            NHWC fp16 [B][H][W][Cp], read by 4-D TMA boxes.
 // Cp = embed padded to 64 (pad lanes hold zeros), head_dim padded to DP = 16/32.
 //
-// Per block (src/cpu.rs:1516-1575): QKV GEMM -> window attention -> proj GEMM with
-// norm1 + residual -> fc1 GEMM + GELU -> fc2 GEMM with norm2 + residual.
+// Per block (src/cpu.rs:1516-1575): QKV GEMM (+ q/k normalisation) -> window
+// attention -> proj GEMM with norm1 + residual -> fused MLP (fc1 + GELU + fc2 + norm2
+// + residual; S2S_UNFUSED_MLP=1 runs it as two GEMMs for validation). Repeated
+// forwards replay a CUDA graph; a sharded forward runs the same code on a row band.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>

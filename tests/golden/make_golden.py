@@ -83,7 +83,8 @@ def write_sw2f(path, h, w, scale, win, x, y, aux):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True,
+                    help="checkout of the swin2sr-rs reference (its tools/network_swin2sr.py)")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.ref) / "tools"))
