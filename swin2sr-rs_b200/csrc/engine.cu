@@ -50,6 +50,8 @@ cudaError_t launch_bicubic(const float* in, float* out, int BC, int h, int w, in
                            cudaStream_t st);
 cudaError_t launch_up2_nhwc(const __half* in, __half* out, int B, int H, int W, int C,
                             cudaStream_t st);
+cudaError_t launch_cpb_table(const float* table, const float* w0, const float* b0, const float* w2,
+                             int heads, int win, int hidden, float* out, cudaStream_t st);
 }  // namespace s2s
 
 using namespace s2s;
@@ -269,7 +271,56 @@ int n_tile_for(int N) {
   return 32;
 }
 
-void build_weights(s2s_handle* H, const TensorTable& T) {
+// The log-spaced relative coordinate table of a win x win window, [(2w-1)^2][2]
+// (network_swin2sr.py:108-120, pretrained window size 0).
+std::vector<float> relative_coords_table(int win) {
+  const int m = 2 * win - 1;
+  std::vector<float> t((size_t)m * m * 2);
+  auto f = [&](int r) {
+    float x = (float)r / (float)(win - 1);
+    x *= 8.0f;
+    const float sgn = x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f);
+    return sgn * std::log2(std::fabs(x) + 1.0f) / std::log2(8.0f);
+  };
+  for (int a = 0; a < m; a++)
+    for (int b = 0; b < m; b++) {
+      t[((size_t)a * m + b) * 2] = f(a - (win - 1));
+      t[((size_t)a * m + b) * 2 + 1] = f(b - (win - 1));
+    }
+  return t;
+}
+
+// One block's bias table from its CPB MLP (cpb_mlp.0: Linear(2, hidden) + ReLU,
+// cpb_mlp.2: Linear(hidden, heads) without bias), computed by k_cpb_table into a
+// device buffer the handle owns. The operands go to `tmp` (freed after the upload sync).
+float* cpb_from_mlp(s2s_handle* H, const TensorTable& T, const std::string& p, int heads,
+                    std::vector<void*>& tmp) {
+  const int win = H->cfg.window, n = win * win;
+  const auto it = T.t.find(p + "attn.cpb_mlp.0.weight");
+  const int hidden = (int)it->second->shape[0];
+  if (it->second->ndim != 2 || it->second->shape[1] != 2 || hidden < 1)
+    fail(S2S_ERR_INVALID, "tensor `" + p + "attn.cpb_mlp.0.weight` must be [hidden][2]");
+  const float* w0 = T.get(p + "attn.cpb_mlp.0.weight", (int64_t)hidden * 2);
+  const float* b0 = T.get(p + "attn.cpb_mlp.0.bias", hidden);
+  const float* w2 = T.get(p + "attn.cpb_mlp.2.weight", (int64_t)heads * hidden);
+  auto dev = [&](const float* src, size_t cnt) {
+    void* d = nullptr;
+    ck(cudaMalloc(&d, cnt * 4), "cpb operands");
+    tmp.push_back(d);
+    ck(cudaMemcpy(d, src, cnt * 4, cudaMemcpyHostToDevice), "cpb operands");
+    return static_cast<const float*>(d);
+  };
+  const std::vector<float> table = relative_coords_table(win);
+  const float* dt = dev(table.data(), table.size());
+  const float* dw0 = dev(w0, (size_t)hidden * 2);
+  const float* db0 = dev(b0, hidden);
+  const float* dw2 = dev(w2, (size_t)heads * hidden);
+  float* out = upload(H, std::vector<float>((size_t)heads * n * n, 0.0f));
+  ck(launch_cpb_table(dt, dw0, db0, dw2, heads, win, hidden, out, 0), "cpb table");
+  return out;
+}
+
+void build_weights(s2s_handle* H, const TensorTable& T, std::vector<void*>& tmp) {
   const s2s_config& c = H->cfg;
   const int C = c.embed, Cp = H->Cp, hd = H->hd, DP = H->DP, heads = H->heads;
   const int HID = c.mlp_ratio * C, HIDp = H->HIDp;
@@ -333,16 +384,21 @@ void build_weights(s2s_handle* H, const TensorTable& T) {
       // cpb_pre [N*N][heads] -> [heads][N][N], key column k of query row q stored at
       // k ^ ((q % 8) * 4) (the attention kernel's shared-memory reads are then free of
       // bank conflicts); logit scale -> exp(min(ls, ln 100)). Both times log2 e: the
-      // attention kernel's softmax is exp2.
+      // attention kernel's softmax is exp2. A checkpoint without the precomputed
+      // table but with the CPB MLP gets the table computed on the device, once.
       const float kLog2e = 1.4426950408889634f;
-      const float* cpb = T.get(p + "attn.cpb_pre", (int64_t)n * n * heads);
-      std::vector<float> cpbt((size_t)heads * n * n, 0.0f);
-      for (int q = 0; q < n; q++)
-        for (int k = 0; k < n; k++)
-          for (int h = 0; h < heads; h++)
-            cpbt[((size_t)h * n + q) * n + (k ^ ((q & 7) << 2))] =
-                cpb[((size_t)q * n + k) * heads + h] * kLog2e;
-      bl.cpb = upload(H, cpbt);
+      if (T.has(p + "attn.cpb_pre") || !T.has(p + "attn.cpb_mlp.0.weight")) {
+        const float* cpb = T.get(p + "attn.cpb_pre", (int64_t)n * n * heads);
+        std::vector<float> cpbt((size_t)heads * n * n, 0.0f);
+        for (int q = 0; q < n; q++)
+          for (int k = 0; k < n; k++)
+            for (int h = 0; h < heads; h++)
+              cpbt[((size_t)h * n + q) * n + (k ^ ((q & 7) << 2))] =
+                  cpb[((size_t)q * n + k) * heads + h] * kLog2e;
+        bl.cpb = upload(H, cpbt);
+      } else {
+        bl.cpb = cpb_from_mlp(H, T, p, heads, tmp);
+      }
       const float* ls = T.get(p + "attn.logit_scale", heads);
       std::vector<float> lse(heads);
       for (int h = 0; h < heads; h++)
@@ -1362,8 +1418,16 @@ int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, 
   for (int i = 0; i < n_tensors; i++) T.t[tensors[i].name] = &tensors[i];
   int rc = guarded(H.get(), [&] {
     ck(cudaStreamCreateWithFlags(&H->stream, cudaStreamNonBlocking), "stream");
-    build_weights(H.get(), T);
-    ck(cudaDeviceSynchronize(), "weight upload");
+    std::vector<void*> tmp;  // device operands of tables computed at upload
+    try {
+      build_weights(H.get(), T, tmp);
+      ck(cudaDeviceSynchronize(), "weight upload");
+    } catch (...) {
+      cudaDeviceSynchronize();
+      for (void* q : tmp) cudaFree(q);
+      throw;
+    }
+    for (void* q : tmp) cudaFree(q);
   });
   if (rc != S2S_OK) {
     g_create_error = H->err;

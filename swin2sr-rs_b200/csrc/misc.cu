@@ -213,6 +213,32 @@ __global__ void k_up2_nhwc(const __half* __restrict__ in, __half* __restrict__ o
   }
 }
 
+// The continuous position bias of one block, computed once on the device from the
+// checkpoint's MLP (network_swin2sr.py:103-137; the table tools/convert.py:141-167
+// precomputes): for query q and key k of a win x win window, relative entry
+// e = (dy + win - 1) * (2 win - 1) + (dx + win - 1) of the log-spaced coordinate table,
+//   cpb[h][q][k] = 16 * sigmoid( sum_j w2[h][j] * relu(w0[j] . t_e + b0[j]) ).
+// Stored as the attention kernel reads it: times log2 e, key column k at
+// k ^ ((q % 8) * 4). Thread per (head, query, key).
+__global__ void k_cpb_table(const float* __restrict__ table, const float* __restrict__ w0,
+                            const float* __restrict__ b0, const float* __restrict__ w2, int heads,
+                            int win, int hidden, float* __restrict__ out) {
+  const int n = win * win;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= heads * n * n) return;
+  const int h = i / (n * n), q = (i / n) % n, k = i % n;
+  const int e = (q / win - k / win + win - 1) * (2 * win - 1) + (q % win - k % win + win - 1);
+  const float t0 = table[2 * e], t1 = table[2 * e + 1];
+  const float* wh = w2 + (size_t)h * hidden;
+  float acc = 0.0f;
+  for (int j = 0; j < hidden; j++) {
+    const float z = t0 * w0[2 * j] + t1 * w0[2 * j + 1] + b0[j];
+    acc += fmaxf(z, 0.0f) * wh[j];
+  }
+  const float v = 16.0f / (1.0f + expf(-acc));
+  out[((size_t)h * n + q) * n + (k ^ ((q & 7) << 2))] = v * 1.4426950408889634f;
+}
+
 inline unsigned grid_for(size_t n, int block) {
   size_t g = (n + block - 1) / block;
   if (g > 148 * 64) g = 148 * 64;
@@ -257,6 +283,13 @@ cudaError_t launch_bicubic(const float* in, float* out, int BC, int h, int w, in
                            cudaStream_t st) {
   return launch_pdl(k_bicubic, dim3(grid_for((size_t)BC * oh * ow, 256)), dim3(256), 0, st, in, out,
                     BC, h, w, oh, ow);
+}
+
+cudaError_t launch_cpb_table(const float* table, const float* w0, const float* b0, const float* w2,
+                             int heads, int win, int hidden, float* out, cudaStream_t st) {
+  const int total = heads * win * win * win * win;
+  k_cpb_table<<<(total + 255) / 256, 256, 0, st>>>(table, w0, b0, w2, heads, win, hidden, out);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_up2_nhwc(const __half* in, __half* out, int B, int H, int W, int C,
