@@ -285,11 +285,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
           tmem_ld32(tbase + c * 32, v);
 #pragma unroll
-          for (int j = 0; j < 32; j++) {
-            float x = pre(v[j], c * 32 + j);
-            if constexpr (RES == 1) x += rpre[c * 32 + j];
-            s1 += x;
-            s2 += x * x;
+          for (int j4 = 0; j4 < 8; j4++) {
+            float4 r4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if constexpr (RES == 1) r4 = reinterpret_cast<const float4*>(rpre + c * 32)[j4];
+            const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+              const int j = 4 * j4 + k;
+              float x = pre(v[j], c * 32 + j);
+              if constexpr (RES == 1) x += rr[k];
+              s1 += x;
+              s2 += x * x;
+            }
           }
         }
         const float nf = (float)e.ln_n;
@@ -324,11 +331,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float4 bb = *reinterpret_cast<const float4*>(s_vec + cl0 + 4 * u);
           float x[4] = {v[4 * u] + bb.x, v[4 * u + 1] + bb.y, v[4 * u + 2] + bb.z,
                         v[4 * u + 3] + bb.w};
+          float4 r4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if constexpr (RES == 1) r4 = reinterpret_cast<const float4*>(rpre + cl0)[u];
+          const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
           for (int k = 0; k < 4; k++) {
             if constexpr (ACT == ACT_GELU) x[k] = gelu_erf(x[k]);
             if constexpr (ACT == ACT_LRELU) x[k] = x[k] < 0.0f ? x[k] * e.slope : x[k];
-            if constexpr (RES == 1) x[k] += rpre[cl0 + 4 * u + k];
+            if constexpr (RES == 1) x[k] += rr[k];
           }
           if constexpr (LN) {
             const float4 gg = *reinterpret_cast<const float4*>(s_vec + BN + cl0 + 4 * u);
