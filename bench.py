@@ -19,7 +19,9 @@ Printed (rank 0, one JSON line): device-resident throughput (`value`, CUDA event
 on the launch stream, L2 flushed between steps outside the timed events), the
 end-to-end throughput through the public host API with host buffers (`e2e`),
 the dominant kernel's roofline, a bounded CPU-oracle baseline, and the SM clocks
-sampled during the timed region.
+sampled during the timed region. On one GPU, `png_e2e` is the CLI's image path:
+PNG bytes in -> PNG bytes out for 8 images, pipelined (host decode, the device
+image path, host deflate), with one image's stages timed alone beside it.
 """
 from __future__ import annotations
 
@@ -394,6 +396,41 @@ def main():
         e2e_s = float(t.item())
     e2e_value = job_mpix / e2e_s
 
+    # ------------------------------------------------ PNG in -> PNG out (one GPU)
+    # The CLI's image path (src/main.rs:205-378) through upscale_pngs: host decode,
+    # s2s_forward_image (sample scaling, Pre::adjust, the forward and the PNG row
+    # filter on the device; only bytes cross PCIe), host deflate; images pipelined.
+    png = None
+    if world == 1 and B == 1:
+        cli = importlib.import_module("swin2sr_b200.cli")
+        image = importlib.import_module("swin2sr_b200.image")
+        src = capi.png_encode_rgb8(image.Image(w, h, x[0]).to_rgb8())
+        n_img = 8
+        cli.upscale_pngs([handle], [src] * 2, batch=1)            # warm: plan + graph
+        st: dict = {}
+        outs, _ = cli.upscale_pngs([handle], [src] * n_img, batch=1, stats=st)
+        samples, depth = capi.png_decode(src)
+        t = time.perf_counter()
+        for _ in range(5):
+            capi.png_decode(src)
+        dec_ms = (time.perf_counter() - t) / 5 * 1e3
+        t = time.perf_counter()
+        for _ in range(5):
+            rows, _ = handle.forward_image(samples[None], depth, png_rows=True)
+        fwd_ms = (time.perf_counter() - t) / 5 * 1e3
+        t = time.perf_counter()
+        for _ in range(3):
+            capi.png_encode_rows(rows[0])
+        enc_ms = (time.perf_counter() - t) / 3 * 1e3
+        png = {"value": round(st["output_mpix"] / st["seconds"], 3), "unit": "Mpix/s",
+               "images": n_img, "host_threads": os.cpu_count(),
+               "png_bytes_in": len(src), "png_bytes_out": len(outs[0]),
+               "h2d_bytes_per_image": int(samples.nbytes),
+               "d2h_bytes_per_image": int(rows.nbytes),
+               "one_image_ms": {"decode": round(dec_ms, 3), "forward_image": round(fwd_ms, 3),
+                                "deflate_all_threads": round(enc_ms, 3)},
+               "zlib_level": "default (6)"}
+
     # ---------------------------------------------------------------- roofline
     pk_burst, pk_sus, hbm, pk_kind = peaks()
     # per launch on this rank: its images, or its band's owned rows
@@ -471,6 +508,7 @@ def main():
                                               * B * 3 * h * w * 4),
                     "d2h_bytes_per_step": int((world if mode == "replicas" else 1)
                                               * B * 3 * h * s * w * s * 4)},
+            "png_e2e": png,
             "roofline": roofline, "whole_forward": whole, "cpu_baseline": cpu,
             "gpu_launches": int(launches), "clocks": clk,
             "kernel_ms_per_step": {k: round(v[1], 4) for k, v in sorted(

@@ -109,7 +109,8 @@ int64_t s2s_uploaded_bytes(const s2s_handle* h);
  * activation bytes a forward of `batch` h x w images allocates. */
 int64_t s2s_workspace_bytes(const s2s_handle* h, int batch, int height, int width);
 
-/* The last error message of `h` (or of the last failed s2s_create when h is NULL). */
+/* The last error message of `h` (or, when h is NULL, of the last failed s2s_create
+ * or handle-less call on this thread). */
 const char* s2s_last_error(const s2s_handle* h);
 
 /* Per-launch CUDA-event timing, the SWIN2SR_PROFILE_GPU profiler
@@ -198,6 +199,60 @@ int s2s_band_halo_ops(int rank, int world, int own_rows, int rows, int cyclic, i
 #define S2S_NOALLOC_MAX_TOKENS 1048576
 int s2s_window_attention_noalloc(s2s_handle* h, int stage, int block, int batch, int hp, int wp,
                                  const void* d_qkv, void* d_out, int ld_out, void* stream);
+
+/* ---- The image path either side of the forward (src/main.rs:205-224, 365-378:
+ * image::load_rgb -> Pre::adjust -> forward -> Image::to_rgb8 -> image::save_rgb).
+ * Handle-less calls report errors through s2s_last_error(NULL). */
+
+/* image::load_rgb's header checks (src/image.rs:49-65): width, height, samples per
+ * pixel (1 grey, 2 grey+alpha, 3 RGB, 4 RGBA) and bit depth (8 or 16). Indexed
+ * colour fails with "unsupported png colour type Indexed", depths below 8 with
+ * "unsupported png bit depth One|Two|Four" (S2S_ERR_INVALID). */
+int s2s_png_header(const void* png, size_t bytes, int* width, int* height, int* channels,
+                   int* bit_depth);
+
+/* Inflate, unfilter and de-interlace (Adam7) into interleaved samples, 16-bit
+ * samples big-endian: the buffer the png crate's next_frame fills
+ * (src/image.rs:50-52). `capacity` must hold width*height*channels*bit_depth/8. */
+int s2s_png_decode(const void* png, size_t bytes, void* samples, size_t capacity);
+
+/* image::save_rgb (src/image.rs:98-114): an 8-bit RGB, non-interlaced PNG of
+ * interleaved `rgb` [height][width][3]. Rows are filtered per row (the filter with
+ * the least sum of |signed byte|); the zlib stream is deflated at `level` (-1..9,
+ * -1 = zlib's default) on `threads` host threads (0 = all cores), each segment
+ * primed with the 32 KiB before it. The file is malloc'd into *png (release it
+ * with s2s_free); the pixels it decodes to are `rgb` exactly. */
+int s2s_png_encode_rgb8(int width, int height, const uint8_t* rgb, int level, int threads,
+                        uint8_t** png, size_t* bytes);
+
+/* The same around rows already filtered (s2s_forward_image with png_rows): per row
+ * one filter-type byte (0-4) and 3*width filtered bytes. */
+int s2s_png_encode_rows(int width, int height, const uint8_t* rows, int level, int threads,
+                        uint8_t** png, size_t* bytes);
+
+void s2s_free(void* p);
+
+/* load_rgb's sample scaling (src/image.rs:62-75) fused with Pre::adjust
+ * (src/backend.rs:76-86) on the device: `d_samples` [batch][h][w][channels] (8-bit,
+ * or 16-bit big-endian) -> `d_chw` [batch][3][h][w] fp32, (s * (1/255 or 1/65535) -
+ * mean) * img_range, each operation rounded separately as the host does. */
+int s2s_adjust_device(const s2s_handle* h, int batch, int height, int width, const void* d_samples,
+                      int channels, int bit_depth, float* d_chw, void* stream);
+
+/* Image::to_rgb8 (src/image.rs:28-39) on the device: [batch][3][h][w] fp32 ->
+ * [batch][h][w][3] bytes (clamp to [0,1], * 255, floor(+0.5); NaN -> 255). With
+ * `png_rows` non-zero the output is PNG scanlines instead, [batch][h][1 + 3w]: per
+ * row the chosen filter type and the filtered bytes, for s2s_png_encode_rows. */
+int s2s_rgb8_device(int batch, int height, int width, const float* d_chw, int png_rows,
+                    uint8_t* d_out, void* stream);
+
+/* The image path in one call, host buffers, synchronous: decoded samples in
+ * ([batch][h][w][channels], 8 or 16 bit), 8-bit RGB out (to_rgb8 layout
+ * [batch][h*s][w*s][3], or PNG scanlines [batch][h*s][1 + 3*w*s] with png_rows).
+ * `aux` (may be NULL; pixelshuffle_aux only) receives the aux plane in the same
+ * format at [batch][hp][wp] (src/main.rs:395-418). Only bytes cross PCIe. */
+int s2s_forward_image(s2s_handle* h, int batch, int height, int width, const void* samples,
+                      int channels, int bit_depth, int png_rows, uint8_t* out, uint8_t* aux);
 
 void s2s_destroy(s2s_handle* h);
 

@@ -194,6 +194,47 @@ def pad_reflect(x: np.ndarray, hp: int, wp: int) -> np.ndarray:
     return out
 
 
+# ---- the image path either side of the forward (numpy: byte and scalar float work)
+
+def load_samples(samples: np.ndarray, channels: int, bit_depth: int) -> np.ndarray:
+    """swin2sr-rs src/image.rs:57-95: decoded PNG samples -> planar f32 [3][h][w].
+
+    `samples` is [h][w][channels * bit_depth / 8] uint8 as the png crate returns it
+    (16-bit samples big-endian). Each sample times the f32 constant 1/255 or 1/65535
+    (`sample_scale`, :62-63); grey and grey+alpha repeat channel 0, RGB(A) take 0..2
+    (:83-91)."""
+    s = np.asarray(samples, np.uint8)
+    h, w, _ = s.shape
+    if bit_depth == 16:
+        v = (s[..., 0::2].astype(np.uint32) << 8) | s[..., 1::2]
+        scale = np.float32(1.0) / np.float32(65535.0)
+    else:
+        v = s.astype(np.uint32)
+        scale = np.float32(1.0) / np.float32(255.0)
+    v = v.reshape(h, w, channels).astype(np.float32) * scale
+    idx = [0, 0, 0] if channels < 3 else [0, 1, 2]
+    return np.ascontiguousarray(np.stack([v[..., i] for i in idx]), dtype=np.float32)
+
+
+def adjust(img: np.ndarray, mean, img_range: float) -> np.ndarray:
+    """swin2sr-rs src/backend.rs:76-86 Pre::adjust: (v - mean[c]) * img_range in f32."""
+    x = np.asarray(img, np.float32)
+    m = np.asarray(mean, np.float32).reshape(3, 1, 1)
+    return ((x - m) * np.float32(img_range)).astype(np.float32)
+
+
+def to_rgb8(img: np.ndarray) -> np.ndarray:
+    """swin2sr-rs src/image.rs:28-39 Image::to_rgb8: planar [3][h][w] f32 ->
+    interleaved [h][w][3] bytes. Per value: clamp to [0,1] (f32::clamp keeps NaN),
+    * 255, + 0.5, floor, min 255 (f32::min returns the non-NaN operand, so NaN ->
+    255), `as u8` (saturating)."""
+    x = np.asarray(img, np.float32)
+    c = np.clip(x, np.float32(0.0), np.float32(1.0))          # NaN stays NaN
+    v = np.floor(c * np.float32(255.0) + np.float32(0.5))      # f32 ops, one rounding each
+    v = np.fmin(v, np.float32(255.0))                          # NaN -> 255
+    return np.ascontiguousarray(v.astype(np.uint8).transpose(1, 2, 0))
+
+
 if __name__ == "__main__":
     print(build(force=True))
     print("threads", max_threads(), os.cpu_count())

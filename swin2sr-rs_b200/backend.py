@@ -66,6 +66,14 @@ class Gpu(Backend):
     def forward_batch(self, x: np.ndarray):
         return self.handle.forward_batch(x)
 
+    def forward_image(self, samples: np.ndarray, bit_depth: int = 8, png_rows: bool = False):
+        """The CLI's image path on the device (src/main.rs:205-378 without the file
+        IO): decoded PNG samples [B][h][w][c] -> to_rgb8 bytes [B][h*s][w*s][3] (or
+        PNG scanlines with png_rows), plus the aux plane for pixelshuffle_aux."""
+        out, aux = self.handle.forward_image(samples, bit_depth, png_rows)
+        self._aux = None
+        return out, aux
+
     def aux(self):
         return self._aux
 

@@ -4,7 +4,7 @@
 
 The library is one unity translation unit (csrc/s2s.cu) compiled for
 sm_100a only, with the C ABI of include/s2s.h; it depends on the CUDA runtime
-(linked statically) and nothing else.
+(linked statically) and zlib (the PNG codec).
 """
 from __future__ import annotations
 
@@ -30,7 +30,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         if LIB.stat().st_mtime >= newest:
             return LIB
     cmd = [NVCC, *FLAGS, "-I", str(ROOT / "include"), "-o", str(LIB) + ".tmp",
-           str(PKG / "csrc" / "s2s.cu")]
+           str(PKG / "csrc" / "s2s.cu"), "-lz"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)

@@ -28,7 +28,9 @@ EXPORTS = ("s2s_create", "s2s_forward", "s2s_forward_batch", "s2s_forward_device
            "s2s_version", "s2s_debug_stop_after", "s2s_debug_read",
            "s2s_window_attention_noalloc", "s2s_band_unique_id", "s2s_band_init",
            "s2s_band_init_local", "s2s_band_rows", "s2s_forward_band", "s2s_forward_band_host",
-           "s2s_band_partition", "s2s_band_halo_ops")
+           "s2s_band_partition", "s2s_band_halo_ops", "s2s_png_header", "s2s_png_decode",
+           "s2s_png_encode_rgb8", "s2s_png_encode_rows", "s2s_free", "s2s_adjust_device",
+           "s2s_rgb8_device", "s2s_forward_image")
 BAND_ID_BYTES = 128
 
 
@@ -115,6 +117,26 @@ def load() -> ctypes.CDLL:
     L.s2s_band_partition.restype = ctypes.c_int
     L.s2s_band_halo_ops.argtypes = [ctypes.c_int] * 5 + [ip, ctypes.c_int]
     L.s2s_band_halo_ops.restype = ctypes.c_int
+    sz = ctypes.c_size_t
+    u8p = ctypes.POINTER(ctypes.c_uint8)
+    L.s2s_png_header.argtypes = [ctypes.c_char_p, sz, ip, ip, ip, ip]
+    L.s2s_png_header.restype = ctypes.c_int
+    L.s2s_png_decode.argtypes = [ctypes.c_char_p, sz, vp, sz]
+    L.s2s_png_decode.restype = ctypes.c_int
+    for f in (L.s2s_png_encode_rgb8, L.s2s_png_encode_rows):
+        f.argtypes = [ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, ctypes.c_int,
+                      ctypes.POINTER(u8p), ctypes.POINTER(sz)]
+        f.restype = ctypes.c_int
+    L.s2s_free.argtypes = [vp]
+    L.s2s_free.restype = None
+    L.s2s_adjust_device.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int,
+                                    ctypes.c_int, vp, vp]
+    L.s2s_adjust_device.restype = ctypes.c_int
+    L.s2s_rgb8_device.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, vp, vp]
+    L.s2s_rgb8_device.restype = ctypes.c_int
+    L.s2s_forward_image.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_int, vp, vp]
+    L.s2s_forward_image.restype = ctypes.c_int
     L.s2s_version.argtypes = []
     L.s2s_version.restype = ctypes.c_char_p
     _lib = L
@@ -270,6 +292,34 @@ class Handle:
     def launch_count(self) -> int:
         return int(self.L.s2s_launch_count(self.h))
 
+    # ---- the image path (PNG samples in, 8-bit RGB out)
+    def forward_image(self, samples: np.ndarray, bit_depth: int = 8, png_rows: bool = False):
+        """s2s_forward_image. `samples` [B][h][w][channels] uint8 (8-bit) or
+        [B][h][w][channels * 2] uint8 (16-bit, big-endian pairs), as png_decode returns
+        them. Returns (out, aux): to_rgb8 bytes [B][h*s][w*s][3] (PNG scanlines
+        [B][h*s][1 + 3*w*s] with png_rows) and the aux plane likewise, or None."""
+        x = np.ascontiguousarray(samples, dtype=np.uint8)
+        B, h, w, cb = x.shape
+        ch = cb // (bit_depth // 8)
+        s, win = self.wt.scale, self.wt.window
+        H, W = h * s, w * s
+        out = np.empty((B, H, 1 + 3 * W) if png_rows else (B, H, W, 3), np.uint8)
+        aux = None
+        if self.wt.upsampler == "pixelshuffle_aux":
+            hp, wp = (h // win + 1) * win, (w // win + 1) * win
+            aux = np.empty((B, hp, 1 + 3 * wp) if png_rows else (B, hp, wp, 3), np.uint8)
+        self._check(self.L.s2s_forward_image(
+            self.h, B, h, w, x.ctypes.data, ch, bit_depth, int(png_rows), out.ctypes.data,
+            aux.ctypes.data if aux is not None else None))
+        return out, aux
+
+    def adjust_device(self, B, h, w, d_samples: int, channels: int, bit_depth: int, d_chw: int,
+                      stream: int = 0):
+        """s2s_adjust_device on device pointers (enqueued, not synchronised)."""
+        self._check(self.L.s2s_adjust_device(self.h, B, h, w, ctypes.c_void_p(d_samples), channels,
+                                             bit_depth, ctypes.c_void_p(d_chw),
+                                             ctypes.c_void_p(stream or None)))
+
 
 def band_unique_id() -> bytes:
     """s2s_band_unique_id: the NCCL id one rank makes and hands to the others."""
@@ -307,3 +357,64 @@ def band_halo_ops(rank: int, world: int, own_rows: int, rows: int, cyclic: bool)
     if k < 0:
         raise S2SError(S2S_ERR_INVALID, "bad halo arguments")
     return [tuple(buf[4 * i:4 * i + 4]) for i in range(k)]
+
+
+# ---- PNG codec and device quantisation (handle-less)
+def _fail(L, rc):
+    if rc != S2S_OK:
+        raise S2SError(rc, L.s2s_last_error(None).decode())
+
+
+def png_header(data: bytes):
+    """(width, height, channels, bit_depth) of a PNG image load_rgb accepts."""
+    L = load()
+    w, h, c, d = (ctypes.c_int() for _ in range(4))
+    _fail(L, L.s2s_png_header(data, len(data), ctypes.byref(w), ctypes.byref(h), ctypes.byref(c),
+                              ctypes.byref(d)))
+    return w.value, h.value, c.value, d.value
+
+
+def png_decode(data: bytes):
+    """Decoded samples [h][w][channels * bit_depth / 8] uint8 and the bit depth."""
+    L = load()
+    w, h, c, d = png_header(data)
+    out = np.empty((h, w, c * (d // 8)), np.uint8)
+    _fail(L, L.s2s_png_decode(data, len(data), out.ctypes.data, out.nbytes))
+    return out, d
+
+
+def _encode(fn, w, h, buf, level, threads) -> bytes:
+    L = load()
+    p = ctypes.POINTER(ctypes.c_uint8)()
+    n = ctypes.c_size_t()
+    _fail(L, fn(w, h, buf.ctypes.data, level, threads, ctypes.byref(p), ctypes.byref(n)))
+    try:
+        return ctypes.string_at(p, n.value)
+    finally:
+        L.s2s_free(p)
+
+
+def png_encode_rgb8(rgb: np.ndarray, level: int = -1, threads: int = 0) -> bytes:
+    """An 8-bit RGB PNG of `rgb` [h][w][3] uint8 (image::save_rgb)."""
+    x = np.ascontiguousarray(rgb, dtype=np.uint8)
+    h, w, c = x.shape
+    if c != 3:
+        raise ValueError("png_encode_rgb8 takes [h][w][3] bytes")
+    return _encode(load().s2s_png_encode_rgb8, w, h, x, level, threads)
+
+
+def png_encode_rows(rows: np.ndarray, level: int = -1, threads: int = 0) -> bytes:
+    """An 8-bit RGB PNG around filtered scanlines [h][1 + 3w] (forward_image png_rows)."""
+    x = np.ascontiguousarray(rows, dtype=np.uint8)
+    h, L1 = x.shape
+    if (L1 - 1) % 3:
+        raise ValueError("scanlines must be 1 + 3 * width bytes")
+    return _encode(load().s2s_png_encode_rows, (L1 - 1) // 3, h, x, level, threads)
+
+
+def rgb8_device(B: int, h: int, w: int, d_chw: int, d_out: int, png_rows: bool = False,
+                stream: int = 0) -> None:
+    """s2s_rgb8_device on device pointers (enqueued, not synchronised)."""
+    L = load()
+    _fail(L, L.s2s_rgb8_device(B, h, w, ctypes.c_void_p(d_chw), int(png_rows),
+                               ctypes.c_void_p(d_out), ctypes.c_void_p(stream or None)))

@@ -163,6 +163,8 @@ struct s2s_handle {
   cudaStream_t stream = nullptr;
   float *h_in = nullptr, *h_out = nullptr, *h_aux = nullptr;  // device staging for host calls
   size_t h_in_n = 0, h_out_n = 0, h_aux_n = 0;
+  uint8_t *b_in = nullptr, *b_out = nullptr;  // device staging of the image calls (bytes)
+  size_t b_in_n = 0, b_out_n = 0;
   bool profiling = false;
   std::string prof_only;  // profile only kernel classes with this prefix
   std::vector<ProfEntry> prof_pending;
@@ -1734,6 +1736,8 @@ void s2s_destroy(s2s_handle* H) {
   if (H->h_in) cudaFree(H->h_in);
   if (H->h_out) cudaFree(H->h_out);
   if (H->h_aux) cudaFree(H->h_aux);
+  if (H->b_in) cudaFree(H->b_in);
+  if (H->b_out) cudaFree(H->b_out);
   if (H->side) cudaStreamDestroy(H->side);
   if (H->fork) cudaEventDestroy(H->fork);
   if (H->join) cudaEventDestroy(H->join);

@@ -5,4 +5,5 @@
 #include "mlp.cu"
 #include "misc.cu"
 #include "engine.cu"
+#include "image.cu"
 #include "noalloc.cu"
