@@ -216,6 +216,62 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return x >= 0.0f ? x - h : h;
 }
 
+// Packed two-lane fp32 arithmetic of sm_100 (add/mul/fma .f32x2): the same IEEE
+// operations as the scalar forms, one instruction for two values.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// gelu_erf of (x0 + b0, x1 + b1): the bias add and the polynomial in packed form,
+// each operation and its order as in gelu_erf, the tail in gelu_erf's own scalar
+// expression.
+__device__ __forceinline__ float2 gelu_erf2(float x0, float x1, float b0, float b1) {
+  const float2 xs = f2_unpack(f2_add(f2_pack(x0, x1), f2_pack(b0, b1)));
+  const unsigned long long t =
+      f2_mul(f2_pack(fabsf(xs.x), fabsf(xs.y)),
+             f2_pack(0.70710678118654752440f, 0.70710678118654752440f));
+  unsigned long long p = f2_pack(0.0000430638f, 0.0000430638f);
+  p = f2_fma(p, t, f2_pack(0.0002765672f, 0.0002765672f));
+  p = f2_fma(p, t, f2_pack(0.0001520143f, 0.0001520143f));
+  p = f2_fma(p, t, f2_pack(0.0092705272f, 0.0092705272f));
+  p = f2_fma(p, t, f2_pack(0.0422820123f, 0.0422820123f));
+  p = f2_fma(p, t, f2_pack(0.0705230784f, 0.0705230784f));
+  p = f2_fma(p, t, f2_pack(1.0f, 1.0f));
+  p = f2_mul(p, p);
+  p = f2_mul(p, p);
+  p = f2_mul(p, p);
+  p = f2_mul(p, p);
+  const float2 pp = f2_unpack(p);
+  float r0, r1;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(pp.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(pp.y));
+  const float h0 = 0.5f * xs.x * r0, h1 = 0.5f * xs.y * r1;
+  return make_float2(xs.x >= 0.0f ? xs.x - h0 : h0, xs.y >= 0.0f ? xs.y - h1 : h1);
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(

@@ -264,8 +264,10 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
 #pragma unroll
           for (int u = 0; u < 8; u++) {
             const float4 bb = *reinterpret_cast<const float4*>(s_vec + col0 + 4 * u);
-            const __half2 h0 = __floats2half2_rn(gelu_erf(v[4 * u] + bb.x), gelu_erf(v[4 * u + 1] + bb.y));
-            const __half2 h1 = __floats2half2_rn(gelu_erf(v[4 * u + 2] + bb.z), gelu_erf(v[4 * u + 3] + bb.w));
+            const float2 g0 = gelu_erf2(v[4 * u], v[4 * u + 1], bb.x, bb.y);
+            const float2 g1 = gelu_erf2(v[4 * u + 2], v[4 * u + 3], bb.z, bb.w);
+            const __half2 h0 = __floats2half2_rn(g0.x, g0.y);
+            const __half2 h1 = __floats2half2_rn(g1.x, g1.y);
             hv[2 * u] = *reinterpret_cast<const uint32_t*>(&h0);
             hv[2 * u + 1] = *reinterpret_cast<const uint32_t*>(&h1);
           }
