@@ -307,22 +307,33 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         }
         if (!mbar_wait(&acc2[db], (uint32_t)((i >> 1) & 1), DEV_TIMEOUT_ACC)) break;
         tc_fence_after();
+        // row sums of x and x^2 in column order (the bias add two lanes at a time)
         float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll 1
         for (int c = 0; c < CP / 32; c++) {
           float v[32];
           tmem_ld32(td2 + (uint32_t)(c * 32), v);
 #pragma unroll
-          for (int jj = 0; jj < 32; jj++) {
-            const float x = v[jj] + s_vec[HP + c * 32 + jj];
-            s1 += x;
-            s2 += x * x;
+          for (int u = 0; u < 8; u++) {
+            const float4 bb = *reinterpret_cast<const float4*>(s_vec + HP + c * 32 + 4 * u);
+            const float2 x0 = f2_unpack(f2_add(f2_pack(v[4 * u], v[4 * u + 1]), f2_pack(bb.x, bb.y)));
+            const float2 x1 =
+                f2_unpack(f2_add(f2_pack(v[4 * u + 2], v[4 * u + 3]), f2_pack(bb.z, bb.w)));
+            s1 += x0.x;
+            s2 += x0.x * x0.x;
+            s1 += x0.y;
+            s2 += x0.y * x0.y;
+            s1 += x1.x;
+            s2 += x1.x * x1.x;
+            s1 += x1.y;
+            s2 += x1.y * x1.y;
           }
         }
         const float nf = (float)a.ln_n;
         const float mean = s1 / nf;
         const float rstd = 1.0f / sqrtf(fmaxf(s2 / nf - mean * mean, 0.0f) + a.ln_eps);
         const float nmr = -mean * rstd;
+        const unsigned long long RS = f2_pack(rstd, rstd), NM = f2_pack(nmr, nmr);
 #pragma unroll 1
         for (int c = half; c < CP / 32; c += 2, jcnt++) {
           const int jb = jcnt & 1;
@@ -355,11 +366,16 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
             const float4 be = *reinterpret_cast<const float4*>(s_vec + HP + 2 * CP + cl0 + 4 * u);
             float4* slot = reinterpret_cast<float4*>(f32 + lane * 32 + ((u ^ sw128) << 2));
             const float4 rr = *slot;
-            float4 o;
-            o.x = fmaf(fmaf(v[4 * u] + bb.x, rstd, nmr), gg.x, be.x) + rr.x;
-            o.y = fmaf(fmaf(v[4 * u + 1] + bb.y, rstd, nmr), gg.y, be.y) + rr.y;
-            o.z = fmaf(fmaf(v[4 * u + 2] + bb.z, rstd, nmr), gg.z, be.z) + rr.z;
-            o.w = fmaf(fmaf(v[4 * u + 3] + bb.w, rstd, nmr), gg.w, be.w) + rr.w;
+            // fma(fma(v + b, rstd, -mean * rstd), gamma, beta) + residual, two lanes at a time
+            unsigned long long lo = f2_add(f2_pack(v[4 * u], v[4 * u + 1]), f2_pack(bb.x, bb.y));
+            unsigned long long hi =
+                f2_add(f2_pack(v[4 * u + 2], v[4 * u + 3]), f2_pack(bb.z, bb.w));
+            lo = f2_add(f2_fma(f2_fma(lo, RS, NM), f2_pack(gg.x, gg.y), f2_pack(be.x, be.y)),
+                        f2_pack(rr.x, rr.y));
+            hi = f2_add(f2_fma(f2_fma(hi, RS, NM), f2_pack(gg.z, gg.w), f2_pack(be.z, be.w)),
+                        f2_pack(rr.z, rr.w));
+            const float2 ol = f2_unpack(lo), oh = f2_unpack(hi);
+            const float4 o = make_float4(ol.x, ol.y, oh.x, oh.y);
             *slot = o;
             v[4 * u] = o.x;
             v[4 * u + 1] = o.y;
