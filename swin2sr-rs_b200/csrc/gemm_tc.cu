@@ -4,7 +4,10 @@
 // blockIdx.x + gridDim.x, ... computing 128 x BN tiles of D = A * B^T in TMEM (fp16
 // operands, fp32 accumulation) with a fused epilogue:
 //   warp 0       TMA producer: A and B K-slices (64 fp16 = one 128-byte swizzle row)
-//                into a STAGES-deep shared-memory ring that runs across tiles;
+//                into a STAGES-deep shared-memory ring that runs across tiles (with
+//                B resident, variants may give A its own AR-deep ring: two tiles of
+//                A in flight, so a tile's loads do not wait for the previous tile's
+//                MMAs to free their slots);
 //   warp 1       allocates TMEM, issues tcgen05.mma (K = 16 per instruction), frees
 //                ring slots with tcgen05.commit, and alternates between two TMEM
 //                accumulators so the next tile's MMAs overlap this tile's epilogue;
@@ -29,15 +32,18 @@ constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
 constexpr int kEpiWarps = 8;
 constexpr int kStageFloats = 32 * 36;  // STORE_SHUFFLE2 staging: 32 rows x 32 cols, 16-B rows
 // Per epilogue warp: two fp32 32x32 tiles (residual in, result out; 128-byte swizzle)
-// and two fp16 32x32 tiles (64-byte swizzle), double-buffered across chunks.
+// and two fp16 32x32 tiles (64-byte swizzle), double-buffered across chunks. Variants
+// whose epilogue writes fp16 only keep just the two fp16 tiles (kWarpBufF16).
 constexpr int kWarpBuf = 2 * 4096 + 2 * 2048;
+constexpr int kWarpBufF16 = 2 * 2048;
 
 template <int BN>
 struct TmemCols {
   static constexpr uint32_t value = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
 };
 
-template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE>
+template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE, int AR = 0,
+          int WB = kWarpBuf>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
            const __grid_constant__ OutMaps om, const GemmArgs a) {
@@ -46,14 +52,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~uintptr_t(1023));
   constexpr int A_BYTES = 128 * 128;
   constexpr int B_BYTES = BN * 128;
+  constexpr int NA = AR > 0 ? AR : STAGES;  // A ring slots (= the ring's barriers)
+  constexpr int F16OFF = WB >= kWarpBuf ? 8192 : 0;  // fp16 tiles within a warp's staging
+  static_assert(WB == kWarpBuf || (WB == kWarpBufF16 && STORE == STORE_ROWS && RES != 2),
+                "fp16-only staging");
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* obuf = sB + STAGES * B_BYTES;                    // [kEpiWarps][kWarpBuf], 1 KB aligned
-  float* s_vec = reinterpret_cast<float*>(obuf + kEpiWarps * kWarpBuf);  // bias, gamma, beta [3][BN]
+  uint8_t* sB = smem + NA * A_BYTES;
+  uint8_t* obuf = sB + STAGES * B_BYTES;                    // [kEpiWarps][WB], 1 KB aligned
+  float* s_vec = reinterpret_cast<float*>(obuf + kEpiWarps * WB);  // bias, gamma, beta [3][BN]
   int* s_rows = reinterpret_cast<int*>(s_vec + 3 * BN);     // shuffle store: per warp, per row
   uint64_t* full = reinterpret_cast<uint64_t*>(s_rows + kEpiWarps * 32 * 4);
-  uint64_t* empty = full + STAGES;
-  uint64_t* accf = empty + STAGES;   // [2] accumulator ready
+  uint64_t* empty = full + NA;
+  uint64_t* accf = empty + NA;       // [2] accumulator ready
   uint64_t* acce = accf + 2;         // [2] accumulator drained
   uint64_t* fin = acce + 2;          // all MMAs of this CTA retired
   uint64_t* bfull = fin + 1;         // resident B (all K-slices) landed
@@ -90,7 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&mapA);
     tma_prefetch_desc(&mapB);
-    for (int s = 0; s < STAGES; s++) {
+    for (int s = 0; s < NA; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -117,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // When all of this CTA's B (its N tile over the whole K) fits the ring's B slots -
   // a GEMM with K <= 64 * STAGES - it is loaded once and stays resident; the ring then
   // streams A only.
-  const bool bres = !a.conv && num_k <= STAGES;
+  const bool bres = !a.conv && num_k <= STAGES;  // AR > 0 launches guarantee it
 
   if (warp == 0) {
     if (lane == 0) {
@@ -132,9 +142,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int m0, bimg, y0, x0;
         coords(t, m0, bimg, y0, x0);
         for (int k = 0; k < num_k; k++, kit++) {
-          const int s = kit % STAGES;
-          if (kit >= STAGES &&
-              !mbar_wait(&empty[s], ((kit / STAGES) - 1) & 1, DEV_TIMEOUT_EMPTY)) {
+          const int s = kit % NA;
+          if (kit >= NA && !mbar_wait(&empty[s], ((kit / NA) - 1) & 1, DEV_TIMEOUT_EMPTY)) {
             ok = false;
             break;
           }
@@ -164,8 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(b * BN);
         for (int k = 0; k < num_k; k++, kit++) {
-          const int s = kit % STAGES;
-          if (!mbar_wait(&full[s], (kit / STAGES) & 1, DEV_TIMEOUT_FULL)) {
+          const int s = kit % NA;
+          if (!mbar_wait(&full[s], (kit / NA) & 1, DEV_TIMEOUT_FULL)) {
             ok = false;
             break;
           }
@@ -201,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       s_vec[2 * BN + c] = (e.ln_n > 0 && col < e.ln_n) ? e.ln_b[col] : 0.0f;
     }
     asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
-    uint8_t* wbuf = obuf + (warp - 2) * kWarpBuf;
+    uint8_t* wbuf = obuf + (warp - 2) * WB;
     float* stg = reinterpret_cast<float*>(wbuf);  // STORE_SHUFFLE2 staging
     uint64_t* wrb = rbar + 2 * (warp - 2);        // this warp's residual barriers
     uint32_t jcnt = 0;                            // chunks this warp has processed (buffer parity)
@@ -310,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = half; c < BN / 32; c += 2, jcnt++) {
         const int jb = jcnt & 1;
         float* f32 = reinterpret_cast<float*>(wbuf + jb * 4096);
-        uint8_t* f16 = wbuf + 8192 + jb * 2048;
+        uint8_t* f16 = wbuf + F16OFF + jb * 2048;
         float v[32];
         tmem_ld32(tbase + c * 32, v);
         if constexpr (RES == 2) {
@@ -360,7 +369,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           v[4 * u + 1] = x[1];
           v[4 * u + 2] = x[2];
           v[4 * u + 3] = x[3];
-          if (e.o32 || e.o32b) *slot = make_float4(x[0], x[1], x[2], x[3]);
+          if constexpr (WB == kWarpBuf) {
+            if (e.o32 || e.o32b) *slot = make_float4(x[0], x[1], x[2], x[3]);
+          }
         }
         if constexpr (ACT == ACT_QKNORM) {
           // one head's q, k or v is one DP-wide group of this row's columns
@@ -550,21 +561,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE>
+template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE, int AR = 0,
+          int WB = kWarpBuf>
 cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const OutMaps& om,
                      const GemmArgs& a, cudaStream_t st) {
-  const size_t smem = 1024 + (size_t)STAGES * (128 * 128 + BN * 128) + kEpiWarps * kWarpBuf +
-                      3 * BN * 4 + kEpiWarps * 32 * 4 * 4 + (2 * STAGES + 6 + 2 * kEpiWarps) * 8 +
+  constexpr int NA = AR > 0 ? AR : STAGES;
+  if (AR > 0 && (a.conv || a.K / 64 > STAGES)) return cudaErrorInvalidValue;  // B not resident
+  if (WB != kWarpBuf && (a.epi.o32 || a.epi.o32b)) return cudaErrorInvalidValue;
+  const size_t smem = 1024 + (size_t)NA * 128 * 128 + (size_t)STAGES * BN * 128 + kEpiWarps * WB +
+                      3 * BN * 4 + kEpiWarps * 32 * 4 * 4 + (2 * NA + 6 + 2 * kEpiWarps) * 8 +
                       16;
   static int ctas = 0;  // resident CTAs per device (SMs x CTAs per SM), one process per GPU
   if (ctas == 0) {
-    cudaError_t err = cudaFuncSetAttribute(k_gemm<BN, STAGES, ACT, LN, RES, STORE>,
+    cudaError_t err = cudaFuncSetAttribute(k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     int dev = 0, sms = 0, occ = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_gemm<BN, STAGES, ACT, LN, RES, STORE>, kThreads, smem);
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB>, kThreads, smem);
     if (err != cudaSuccess) return err;
     if (occ < 1) return cudaErrorInvalidConfiguration;
     ctas = sms * occ;
@@ -575,7 +590,7 @@ cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const Out
   long G = tiles < ctas ? tiles : ctas;
   G = (G / NT) * NT;
   if (G < NT) G = NT;
-  return launch_pdl(k_gemm<BN, STAGES, ACT, LN, RES, STORE>, dim3((unsigned)G), dim3(kThreads), smem,
+  return launch_pdl(k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB>, dim3((unsigned)G), dim3(kThreads), smem,
                     st, mapA, mapB, om, a);
 }
 
@@ -607,7 +622,9 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   S2S_VARIANT(192, 3, ACT_NONE, false, 1, STORE_ROWS)
   S2S_VARIANT(192, 3, ACT_NONE, true, 1, STORE_ROWS)
   S2S_VARIANT(192, 3, ACT_NONE, false, 2, STORE_ROWS)
-  S2S_VARIANT(192, 3, ACT_QKNORM, false, 0, STORE_ROWS)
+  // QKV (fp16 output only, B resident): A gets a six-slot ring of its own
+  if (BN == 192 && act == ACT_QKNORM && !ln && res == 0 && store == STORE_ROWS)
+    return launch_t<192, 3, ACT_QKNORM, false, 0, STORE_ROWS, 6, kWarpBufF16>(mapA, mapB, om, a, st);
   S2S_VARIANT(96, 4, ACT_QKNORM, false, 0, STORE_ROWS)
   // embed 60 (Cp 64) and the 64-channel head convs
   S2S_VARIANT(64, 4, ACT_NONE, false, 0, STORE_ROWS)
