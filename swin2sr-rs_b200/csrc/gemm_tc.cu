@@ -615,6 +615,9 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   const int res = e.res_pre ? 1 : (e.res_post ? 2 : 0);
   const int store = e.store;
   // embed 180 (Cp 192): QKV, convs, fc1, proj/fc2, patch_embed, stage tail, body skip
+  // the RSTB conv3x3 (fp16 output only): fp16-only staging leaves room for a 4th stage
+  if (BN == 192 && act == ACT_NONE && !ln && res == 0 && store == STORE_ROWS && !e.o32 && !e.o32b)
+    return launch_t<192, 4, ACT_NONE, false, 0, STORE_ROWS, 0, kWarpBufF16>(mapA, mapB, om, a, st);
   S2S_VARIANT(192, 3, ACT_NONE, false, 0, STORE_ROWS)
   S2S_VARIANT(192, 3, ACT_GELU, false, 0, STORE_ROWS)
   S2S_VARIANT(192, 3, ACT_NONE, true, 2, STORE_ROWS)
