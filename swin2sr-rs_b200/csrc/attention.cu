@@ -79,7 +79,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 
 // DP: padded head dim (16 or 32); HPC heads per CTA. Window of 64 tokens (win = 8).
 template <int DP, int HPC>
-__global__ void __launch_bounds__(128 * HPC + 32) k_window_attention(
+__global__ void __launch_bounds__(128 * HPC + 32, HPC == 1 ? 5 : 1) k_window_attention(
     const __half* __restrict__ qkv, __half* __restrict__ out, const float* __restrict__ cpb,
     const int* __restrict__ rows, int heads, int hd, int ld_out,
     int nwh, int nww, int hp, int wp, int shift, int nwin_total, int wh_off) {
