@@ -54,8 +54,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int B_BYTES = BN * 128;
   constexpr int NA = AR > 0 ? AR : STAGES;  // A ring slots (= the ring's barriers)
   constexpr int F16OFF = WB >= kWarpBuf ? 8192 : 0;  // fp16 tiles within a warp's staging
-  static_assert(WB == kWarpBuf || (WB == kWarpBufF16 && STORE == STORE_ROWS && RES != 2),
-                "fp16-only staging");
+  static_assert(WB == kWarpBuf || (WB == kWarpBufF16 && STORE == STORE_ROWS && RES != 2) ||
+                    (WB == kStageFloats * 4 && STORE == STORE_SHUFFLE2),
+                "fp16-only staging, or the pixel-shuffle transpose tile alone");
   uint8_t* sA = smem;
   uint8_t* sB = smem + NA * A_BYTES;
   uint8_t* obuf = sB + STAGES * B_BYTES;                    // [kEpiWarps][WB], 1 KB aligned
@@ -640,8 +641,14 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   S2S_VARIANT(96, 4, ACT_NONE, false, 0, STORE_ROWS)
   S2S_VARIANT(128, 3, ACT_GELU, false, 0, STORE_ROWS)
   // x2 octave convs with the pixel-shuffle store (+ the compressed head's bicubic add)
-  S2S_VARIANT(256, 2, ACT_NONE, false, 0, STORE_SHUFFLE2)
-  S2S_VARIANT(256, 2, ACT_NONE, false, 2, STORE_SHUFFLE2)
+  // the pixel-shuffle store stages one 32 x 32 transpose tile per warp, so a third
+  // ring stage fits
+  if (BN == 256 && act == ACT_NONE && !ln && res == 0 && store == STORE_SHUFFLE2)
+    return launch_t<256, 3, ACT_NONE, false, 0, STORE_SHUFFLE2, 0, kStageFloats * 4>(mapA, mapB, om,
+                                                                                  a, st);
+  if (BN == 256 && act == ACT_NONE && !ln && res == 2 && store == STORE_SHUFFLE2)
+    return launch_t<256, 3, ACT_NONE, false, 2, STORE_SHUFFLE2, 0, kStageFloats * 4>(mapA, mapB, om,
+                                                                                  a, st);
   // 3-channel outputs
   S2S_VARIANT(32, 4, ACT_NONE, false, 0, STORE_PLANES)
   S2S_VARIANT(32, 4, ACT_NONE, false, 0, STORE_DIRECT)
