@@ -360,3 +360,80 @@ def test_cli_refuses_aux_for_a_single_output_head(tmp_path, capsys):
                    "--aux", str(tmp_path / "a.png"), "-q"])
     assert rc == 1
     assert "only the compressed_sr head" in capsys.readouterr().err
+
+
+class _FakeWeights:
+    window, scale = 8, 2
+
+    def __init__(self, upsampler):
+        self.upsampler = upsampler
+
+
+class _FakeHandle:
+    """Stands in for capi.Handle in the driver's host logic: "upscales" by pixel
+    repetition and returns PNG scanlines with filter type 0 (no GPU involved)."""
+
+    def __init__(self, upsampler="pixelshuffle", fail_on=None):
+        self.wt = _FakeWeights(upsampler)
+        self.calls = []
+        self.fail_on = fail_on
+
+    def forward_image(self, samples, bit_depth=8, png_rows=False):
+        assert png_rows
+        B, h, w, cb = samples.shape
+        self.calls.append((B, h, w, cb, bit_depth))
+        if self.fail_on is not None and (h, w) == self.fail_on:
+            raise RuntimeError("fake device failure")
+        ch = cb // (bit_depth // 8)
+        px = samples[..., ::bit_depth // 8][..., :ch]          # high bytes of 16-bit samples
+        rgb = px if ch >= 3 else np.repeat(px[..., :1], 3, axis=-1)
+        rgb = np.ascontiguousarray(rgb[..., :3])
+        up = rgb.repeat(2, axis=1).repeat(2, axis=2)
+        rows = np.zeros((B, 2 * h, 1 + 6 * w), np.uint8)
+        rows[:, :, 1:] = up.reshape(B, 2 * h, 6 * w)
+        aux = None
+        if self.wt.upsampler == "pixelshuffle_aux":
+            aux = np.zeros((B, h, 1 + 3 * w), np.uint8)
+            aux[:, :, 1:] = rgb.reshape(B, h, 3 * w)
+        return rows, aux
+
+
+def test_upscale_pngs_orders_batches_and_aux_on_the_host():
+    cli = cli_mod()
+    imgs = [smooth_rgb(16, 16, 1), smooth_rgb(16, 24, 2), smooth_rgb(16, 16, 3),
+            smooth_rgb(16, 16, 4), smooth_rgb(16, 24, 5)]
+    pngs = [pil_png(a, "RGB") for a in imgs]
+    grey = np.random.default_rng(6).integers(0, 65536, (16, 16), dtype=np.uint16)
+    buf = io.BytesIO()
+    PILImage.fromarray(grey).save(buf, format="PNG")            # 16-bit grey
+    pngs.append(buf.getvalue())
+    hs = [_FakeHandle("pixelshuffle_aux"), _FakeHandle("pixelshuffle_aux")]
+    stats = {}
+    outs, auxs = cli.upscale_pngs(hs, pngs, batch=2, threads=3, want_aux=True, stats=stats)
+    assert stats["images"] == 6 and stats["batches"] == 4
+    assert stats["output_mpix"] == pytest.approx(sum(a.shape[0] * a.shape[1] * 4 for a in imgs
+                                                     + [grey]) / 1e6)
+    calls = sorted(c for h in hs for c in h.calls)
+    assert calls == sorted([(2, 16, 16, 3, 8), (1, 16, 16, 3, 8), (2, 16, 24, 3, 8),
+                            (1, 16, 16, 2, 16)])
+    for a, o, x in zip(imgs, outs, auxs):
+        assert np.array_equal(np.array(PILImage.open(io.BytesIO(o))),
+                              a.repeat(2, axis=0).repeat(2, axis=1))
+        assert np.array_equal(np.array(PILImage.open(io.BytesIO(x))), a)
+    g8 = (grey >> 8).astype(np.uint8)
+    assert np.array_equal(np.array(PILImage.open(io.BytesIO(outs[-1]))),
+                          np.repeat(g8[..., None], 3, -1).repeat(2, axis=0).repeat(2, axis=1))
+    # without --aux nothing is encoded for it
+    outs2, auxs2 = cli.upscale_pngs([_FakeHandle("pixelshuffle_aux")], pngs[:2], batch=4)
+    assert auxs2 == [None, None] and outs2[0] == outs[0]
+
+
+def test_upscale_pngs_reports_device_errors_and_small_images():
+    cli = cli_mod()
+    pngs = [pil_png(smooth_rgb(16, 16, 1), "RGB"), pil_png(smooth_rgb(16, 24, 2), "RGB")]
+    with pytest.raises(RuntimeError, match="fake device failure"):
+        cli.upscale_pngs([_FakeHandle(fail_on=(16, 24))], pngs, batch=1, threads=2)
+    with pytest.raises(ValueError, match="smaller than one 8x8 window"):
+        cli.upscale_pngs([_FakeHandle()], [pil_png(smooth_rgb(7, 16, 3), "RGB")])
+    with pytest.raises(ValueError):
+        cli.upscale_pngs([], pngs)
