@@ -57,7 +57,7 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// 2^x by the SFU (the instruction __expf is built on, without its scaling multiply).
+// 2^x by the SFU: PTX ex2.approx (the logits are pre-scaled by log2 e).
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
