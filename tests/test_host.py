@@ -166,3 +166,29 @@ def test_gelu_erf_approximation_bound():
     got = np.where(x >= 0, x - h, h).astype(np.float64)
     ref = np.array([0.5 * float(v) * (1 + math.erf(float(v) / math.sqrt(2))) for v in x])
     assert np.abs(got - ref).max() < 1e-6
+
+
+def test_bench_kernel_accounting_adds_up_to_the_forward():
+    """bench.py's per-launch FLOPs of each kernel class (the roofline's numerator),
+    summed over one classical-x4 forward's launches, equal the model's algorithmic
+    FLOPs; the MLP's algorithmic bytes are 12 bytes per padded channel per token."""
+    import importlib.util
+    P = pkg()
+    spec = importlib.util.spec_from_file_location("s2s_bench", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    wt = P.weights.Weights.seeded("classical_sr", 0)
+    hp, wp = 248, 328
+    f = bench.kernel_flops(wt, 1, hp, wp)
+    blocks, stages = sum(wt.depths), len(wt.depths)
+    per_forward = {"gemm_qkv": blocks, "window_attention": blocks, "gemm_proj": blocks,
+                   "mlp_fused": blocks, "conv_stage": stages, "gemm_stage_pe": stages,
+                   "gemm_patch_embed": 1, "conv_after_body": 1, "conv_first": 1,
+                   "conv_before_upsample": 1, "conv_upsample0": 1, "conv_upsample1": 1,
+                   "conv_last": 1}
+    total = sum(f[k] * n for k, n in per_forward.items())
+    assert total == wt.flops_forward(hp, wp)
+    # the fused MLP counts fc1 + fc2, the unfused classes the same work split in two
+    assert f["mlp_fused"] == f["gemm_fc1"] + f["gemm_fc2"]
+    T, Cp = hp * wp, 192
+    assert bench.kernel_bytes(wt, 1, hp, wp)["mlp_fused"] == T * Cp * 12
