@@ -133,6 +133,8 @@ struct Plan {
   int* rows[2] = {nullptr, nullptr};  // window-major token -> image row, shift 0 / win/2
   CUtensorMap mF0h, mX16, mAO, mH16, cX16, cAO, cHA;
   CUtensorMap cHB[3][3];  // head planes at 1x, 2x, 4x resolution
+  CUtensorMap cHBp[3][3];                 // the same planes in (boxh + 2)-row patches
+  bool hbp[3][3] = {{false}};             // ... when the plane's conv box allows them
   // Output / residual TMA maps, built on first use for each (buffer, geometry).
   std::map<std::array<int64_t, 8>, CUtensorMap> omaps;
 };
@@ -173,6 +175,7 @@ struct s2s_handle {
   long long launches = 0;
   bool fused_mlp = false;      // (Cp, HIDp) has a fused MLP kernel
   bool graphs = true;          // replay repeated forwards as CUDA graphs (S2S_GRAPHS=0: off)
+  bool no_patch = false;       // conv_last from nine tap boxes (S2S_NO_PATCH=1: validation)
   long long stop_after = -1;   // diagnostics: launches per forward before stopping
   long long fwd_launches = 0;  // launches enqueued by the forward in flight
   // Row-band sharding (s2s_band_init / s2s_band_init_local): this handle's rank.
@@ -665,6 +668,9 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
       int bw, bh;
       conv_box(wp * f, &bw, &bh);
       ok &= make_map_nhwc(&P->cHB[i][r], P->HB[i], B, P->head_rows * f, wp * f, 64, bw, bh);
+      P->hbp[i][r] = bw <= 32 && bw % 8 == 0 &&
+                     make_map_nhwc(&P->cHBp[i][r], P->HB[i], B, P->head_rows * f, wp * f, 64,
+                                   bw, bh + 2);
     }
   if (!ok) {
     free_plan(*P);
@@ -1101,7 +1107,9 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.ld16 = F;
     conv_to("conv_before_upsample", P->cAO, H->cbu, hh0, wp, Cp, e);
   };
-  auto final_planes = [&](const CUtensorMap& mapA, int Hh, int Ww) {
+  // conv_last over head plane HB[i] at resolution 2^r: from kx patches of the plane
+  // when its conv box allows them (three input fetches per tile instead of nine)
+  auto final_planes = [&](int i, int r, int Hh, int Ww) {
     Epi e = epi0();
     e.bias = H->last.b;
     e.store = STORE_PLANES;
@@ -1110,7 +1118,15 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.crop_h = P->crop_rows * s;
     e.crop_w = w * s;
     set_final(H, e);
-    conv_to("conv_last", mapA, H->last, Hh, Ww, F, e);
+    if (!P->hbp[i][r] || H->no_patch) {
+      conv_to("conv_last", P->cHB[i][r], H->last, Hh, Ww, F, e);
+      return;
+    }
+    GemmArgs a = conv_args(B, Hh, Ww, F, H->last.N, e, 0, Hh);
+    a.patch = 1;
+    L.run("conv_last", [&] {
+      return launch_gemm(P->cHBp[i][r], H->last.map, out_maps(P, a), a, H->last.BN, st);
+    });
   };
   switch (c.upsampler) {
     case S2S_PIXELSHUFFLE:
@@ -1156,7 +1172,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         ww *= 2;
         src = &P->cHB[o % 2][o + 1];
       }
-      final_planes(*src, hh, ww);
+      final_planes((octs - 1) % 2, octs, hh, ww);
       break;
     }
     case S2S_PIXELSHUFFLEDIRECT: {
@@ -1204,7 +1220,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.ld16 = F;
         conv_to("conv_hr", P->cHB[2][2], H->hr, 4 * hh0, 4 * wp, F, e);
       }
-      final_planes(P->cHB[0][2], 4 * hh0, 4 * wp);
+      final_planes(0, 2, 4 * hh0, 4 * wp);
       break;
     }
     default:
@@ -1413,6 +1429,8 @@ int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, 
   {
     const char* f = getenv("S2S_UNFUSED_MLP");  // validation switch: the two-GEMM MLP path
     if (f && *f && strcmp(f, "0") != 0) H->fused_mlp = false;
+    const char* np = getenv("S2S_NO_PATCH");  // validation switch: conv_last by tap boxes
+    H->no_patch = np && strcmp(np, "1") == 0;
     const char* g = getenv("S2S_GRAPHS");
     if (g && strcmp(g, "0") == 0) H->graphs = false;
   }

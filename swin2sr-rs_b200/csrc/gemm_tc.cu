@@ -20,7 +20,10 @@
 // In conv mode the A tile is a boxh x boxw patch of output pixels and each K-slice
 // is one (tap, 64-channel chunk) of the NHWC input, fetched by a 4-D TMA box at
 // the tap's offset: TMA's zero fill outside the plane IS the conv's zero padding,
-// so no im2col buffer exists.
+// so no im2col buffer exists. With PATCH (64 input channels), a slot instead holds
+// one (boxh + 2)-row patch per kx and the weights of its three ky taps: tap (ky, kx)
+// is the patch from row ky * boxw on, so the input is fetched three times per tile
+// instead of nine.
 #include "common.cuh"
 #include "gemm_tc.cuh"
 
@@ -43,7 +46,7 @@ struct TmemCols {
 };
 
 template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE, int AR = 0,
-          int WB = kWarpBuf>
+          int WB = kWarpBuf, bool PATCH = false>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
            const __grid_constant__ OutMaps om, const GemmArgs a) {
@@ -53,13 +56,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int A_BYTES = 128 * 128;
   constexpr int B_BYTES = BN * 128;
   constexpr int NA = AR > 0 ? AR : STAGES;  // A ring slots (= the ring's barriers)
+  // a slot's A and B bytes: one K-slice, or with PATCH a (boxh + 2) x boxw patch (at
+  // most 24 KB for boxw <= 32) and three taps' weights
+  constexpr int A_SLOT = PATCH ? 24576 : A_BYTES;
+  constexpr int B_SLOT = PATCH ? 3 * B_BYTES : B_BYTES;
+  static_assert(!PATCH || (AR == 0 && STORE == STORE_PLANES), "patch mode: plane store only");
   constexpr int F16OFF = WB >= kWarpBuf ? 8192 : 0;  // fp16 tiles within a warp's staging
   static_assert(WB == kWarpBuf || (WB == kWarpBufF16 && STORE == STORE_ROWS && RES != 2) ||
-                    (WB == kStageFloats * 4 && STORE == STORE_SHUFFLE2),
-                "fp16-only staging, or the pixel-shuffle transpose tile alone");
+                    (WB == kStageFloats * 4 && STORE == STORE_SHUFFLE2) ||
+                    (WB == 0 && STORE == STORE_PLANES),
+                "fp16-only staging, the pixel-shuffle transpose tile alone, or none for the "
+                "plane store (registers to global)");
   uint8_t* sA = smem;
-  uint8_t* sB = smem + NA * A_BYTES;
-  uint8_t* obuf = sB + STAGES * B_BYTES;                    // [kEpiWarps][WB], 1 KB aligned
+  uint8_t* sB = smem + NA * A_SLOT;
+  uint8_t* obuf = sB + STAGES * B_SLOT;                     // [kEpiWarps][WB], 1 KB aligned
   float* s_vec = reinterpret_cast<float*>(obuf + kEpiWarps * WB);  // bias, gamma, beta [3][BN]
   int* s_rows = reinterpret_cast<int*>(s_vec + 3 * BN);     // shuffle store: per warp, per row
   uint64_t* full = reinterpret_cast<uint64_t*>(s_rows + kEpiWarps * 32 * 4);
@@ -80,7 +90,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = tiles_m * NT;
   const int G = gridDim.x;  // a multiple of NT: the CTA's N tile is fixed
   const int n0 = (blockIdx.x % NT) * BN;
-  const int num_k = a.conv ? 9 * a.kc : a.K / 64;
+  const int num_k = PATCH ? 3 : a.conv ? 9 * a.kc : a.K / 64;  // K-slices (PATCH: kx) per tile
   auto coords = [&](int t, int& m0, int& bimg, int& y0, int& x0) {
     const int mt = t / NT;
     m0 = 0;
@@ -148,16 +158,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], bres ? A_BYTES : A_BYTES + B_BYTES);
-          if (!a.conv) {
-            tma_load_2d(sA + s * A_BYTES, &mapA, &full[s], k * 64, m0);
+          if constexpr (PATCH) {
+            // the patch of kx = k: rows y0 - 1 .. y0 + boxh, columns x0 + k - 1 .. ,
+            // and the weights of taps (0, k), (1, k), (2, k)
+            mbar_arrive_expect_tx(&full[s], (uint32_t)((a.boxh + 2) * a.boxw * 128 + B_SLOT));
+            tma_load_4d(sA + s * A_SLOT, &mapA, &full[s], 0, x0 + k - 1, y0 - 1, bimg);
+            for (int ky = 0; ky < 3; ky++)
+              tma_load_2d(sB + s * B_SLOT + ky * B_BYTES, &mapB, &full[s], (ky * 3 + k) * 64, n0);
           } else {
-            const int tap = k / a.kc, cc = k - tap * a.kc;
-            const int ky = tap / 3, kx = tap - ky * 3;
-            tma_load_4d(sA + s * A_BYTES, &mapA, &full[s], cc * 64, x0 + kx - 1, y0 + ky - 1,
-                        bimg);
+            mbar_arrive_expect_tx(&full[s], bres ? A_BYTES : A_BYTES + B_BYTES);
+            if (!a.conv) {
+              tma_load_2d(sA + s * A_SLOT, &mapA, &full[s], k * 64, m0);
+            } else {
+              const int tap = k / a.kc, cc = k - tap * a.kc;
+              const int ky = tap / 3, kx = tap - ky * 3;
+              tma_load_4d(sA + s * A_SLOT, &mapA, &full[s], cc * 64, x0 + kx - 1, y0 + ky - 1,
+                          bimg);
+            }
+            if (!bres) tma_load_2d(sB + s * B_SLOT, &mapB, &full[s], k * 64, n0);
           }
-          if (!bres) tma_load_2d(sB + s * B_BYTES, &mapB, &full[s], k * 64, n0);
         }
       }
     }
@@ -180,12 +199,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t ad = sw128_desc(smem_u32(sA + s * A_BYTES));
-          const uint64_t bd = sw128_desc(smem_u32(sB + (bres ? k : s) * B_BYTES));
+          if constexpr (PATCH) {
+            // tap (ky, k): the patch from row ky * boxw on (1024-byte aligned: boxw % 8 == 0)
+            for (int ky = 0; ky < 3; ky++) {
+              const uint64_t ad = sw128_desc(smem_u32(sA + s * A_SLOT + ky * a.boxw * 128));
+              const uint64_t bd = sw128_desc(smem_u32(sB + s * B_SLOT + ky * B_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < 4; kk++) {
-            tc_mma_f16(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
-                       (k | kk) != 0 ? 1u : 0u);
+              for (int kk = 0; kk < 4; kk++)
+                tc_mma_f16(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                           (k | ky | kk) != 0 ? 1u : 0u);
+            }
+          } else {
+            const uint64_t ad = sw128_desc(smem_u32(sA + s * A_SLOT));
+            const uint64_t bd = sw128_desc(smem_u32(sB + (bres ? k : s) * B_SLOT));
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+              tc_mma_f16(d, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), idesc,
+                         (k | kk) != 0 ? 1u : 0u);
+            }
           }
           tc_commit(&empty[s]);
         }
@@ -563,24 +594,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE, int AR = 0,
-          int WB = kWarpBuf>
+          int WB = kWarpBuf, bool PATCH = false>
 cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const OutMaps& om,
                      const GemmArgs& a, cudaStream_t st) {
   constexpr int NA = AR > 0 ? AR : STAGES;
+  constexpr size_t A_SLOT = PATCH ? 24576 : 128 * 128, B_SLOT = (PATCH ? 3 : 1) * BN * 128;
+  if (PATCH && (!a.conv || a.kc != 1 || a.boxw > 32 || a.boxw % 8 || a.boxh + 2 > 256))
+    return cudaErrorInvalidValue;
   if (AR > 0 && (a.conv || a.K / 64 > STAGES)) return cudaErrorInvalidValue;  // B not resident
   if (WB != kWarpBuf && (a.epi.o32 || a.epi.o32b)) return cudaErrorInvalidValue;
-  const size_t smem = 1024 + (size_t)NA * 128 * 128 + (size_t)STAGES * BN * 128 + kEpiWarps * WB +
+  const size_t smem = 1024 + (size_t)NA * A_SLOT + (size_t)STAGES * B_SLOT + kEpiWarps * WB +
                       3 * BN * 4 + kEpiWarps * 32 * 4 * 4 + (2 * NA + 6 + 2 * kEpiWarps) * 8 +
                       16;
   static int ctas = 0;  // resident CTAs per device (SMs x CTAs per SM), one process per GPU
   if (ctas == 0) {
-    cudaError_t err = cudaFuncSetAttribute(k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB>,
+    cudaError_t err = cudaFuncSetAttribute(k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     int dev = 0, sms = 0, occ = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB>, kThreads, smem);
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH>, kThreads, smem);
     if (err != cudaSuccess) return err;
     if (occ < 1) return cudaErrorInvalidConfiguration;
     ctas = sms * occ;
@@ -591,7 +625,7 @@ cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const Out
   long G = tiles < ctas ? tiles : ctas;
   G = (G / NT) * NT;
   if (G < NT) G = NT;
-  return launch_pdl(k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB>, dim3((unsigned)G), dim3(kThreads), smem,
+  return launch_pdl(k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH>, dim3((unsigned)G), dim3(kThreads), smem,
                     st, mapA, mapB, om, a);
 }
 
@@ -615,6 +649,11 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   const bool ln = e.ln_n > 0;
   const int res = e.res_pre ? 1 : (e.res_post ? 2 : 0);
   const int store = e.store;
+  if (a.patch) {  // conv_last: kx patches, five slots (the plane store needs no staging)
+    if (BN == 32 && act == ACT_NONE && !ln && res == 0 && store == STORE_PLANES)
+      return launch_t<32, 5, ACT_NONE, false, 0, STORE_PLANES, 0, 0, true>(mapA, mapB, om, a, st);
+    return cudaErrorNotSupported;
+  }
   // embed 180 (Cp 192): QKV, convs, fc1, proj/fc2, patch_embed, stage tail, body skip
   // the RSTB conv3x3 (fp16 output only): fp16-only staging leaves room for a 4th stage
   if (BN == 192 && act == ACT_NONE && !ln && res == 0 && store == STORE_ROWS && !e.o32 && !e.o32b)

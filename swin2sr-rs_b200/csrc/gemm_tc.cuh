@@ -69,6 +69,9 @@ struct GemmArgs {
   int y_off, y_end;  // conv: output rows [y_off, y_end) of the H-row plane (rows outside
                      // are read as the 3x3 halo only)
   int kc;  // conv: 64-channel chunks per tap
+  // conv with kc == 1 and boxw <= 32: mapA's boxes are (boxh + 2)-row patches, one per
+  // kx, each serving its three ky taps (launch_gemm supports it for the plane store)
+  int patch;
   Epi epi;
 };
 

@@ -242,6 +242,33 @@ def test_unfused_mlp_path_matches_the_fused_kernel(task, monkeypatch):
     assert err <= 1e-4
 
 
+@pytest.mark.parametrize("task,h,w", [("classical_sr", 33, 41), ("classical_sr_x2", 29, 37),
+                                      ("real_sr", 21, 26), ("compressed_sr", 17, 22)])
+def test_conv_last_patches_match_the_tap_boxes(task, h, w, monkeypatch):
+    """conv_last reads its input as three kx patches per tile (each serving its three
+    ky taps) unless S2S_NO_PATCH=1 (read at create) asks for the nine tap boxes; the
+    same fp16 operands summed in another tap order, so the outputs agree to fp32
+    rounding."""
+    capi = importlib.import_module("swin2sr_b200.capi")
+    P = pkg()
+    wt = P.weights.Weights.seeded(task, 0, True)
+    x = adjust(wt, np.random.default_rng(23).random((1, 3, h, w), dtype=np.float32))
+    H = capi.Handle(wt)
+    try:
+        got = H.forward_batch(x)[0]
+    finally:
+        H.close()
+    monkeypatch.setenv("S2S_NO_PATCH", "1")
+    H = capi.Handle(wt)
+    try:
+        ref = H.forward_batch(x)[0]
+    finally:
+        H.close()
+    err = float(np.abs(got - ref).max())
+    print(f"{task}: patched vs tap-box conv_last max-abs {err:.3e}")
+    assert err <= 1e-5
+
+
 def test_cpb_table_computed_on_device_from_the_mlp():
     """A checkpoint with the CPB MLP (cpb_mlp.0 / cpb_mlp.2) instead of the converter's
     precomputed cpb_pre gets each block's bias table computed on the device at
