@@ -1098,6 +1098,18 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     GemmArgs a = conv_args(B, Hh, Ww, Cip, tw.N, e, 0, Hh);
     L.run(name, [&] { return launch_gemm(mapA, tw.map, out_maps(P, a), a, tw.BN, st); });
   };
+  // a 64-channel conv over head plane HB[i] at resolution 2^r, from kx patches when
+  // the plane's conv box allows them
+  auto conv_plane = [&](const char* name, int i, int r, const TcWeight& tw, int Hh, int Ww,
+                        Epi e) {
+    if (!P->hbp[i][r] || H->no_patch) {
+      conv_to(name, P->cHB[i][r], tw, Hh, Ww, F, e);
+      return;
+    }
+    GemmArgs a = conv_args(B, Hh, Ww, F, tw.N, e, 0, Hh);
+    a.patch = 1;
+    L.run(name, [&] { return launch_gemm(P->cHBp[i][r], tw.map, out_maps(P, a), a, tw.BN, st); });
+  };
   auto cbu = [&]() {
     Epi e = epi0();
     e.bias = H->cbu.b;
@@ -1198,7 +1210,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.slope = 0.2f;
         e.o16 = P->HB[1];
         e.ld16 = F;
-        conv_to("conv_up1", P->cHB[0][1], H->up1, 2 * hh0, 2 * wp, F, e);
+        conv_plane("conv_up1", 0, 1, H->up1, 2 * hh0, 2 * wp, e);
       }
       L.run("upsample_nearest",
             [&] { return launch_up2_nhwc(P->HB[1], P->HB[0], B, 2 * hh0, 2 * wp, F, st); });
@@ -1209,7 +1221,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.slope = 0.2f;
         e.o16 = P->HB[2];
         e.ld16 = F;
-        conv_to("conv_up2", P->cHB[0][2], H->up2, 4 * hh0, 4 * wp, F, e);
+        conv_plane("conv_up2", 0, 2, H->up2, 4 * hh0, 4 * wp, e);
       }
       {
         Epi e = epi0();
@@ -1218,7 +1230,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.slope = 0.2f;
         e.o16 = P->HB[0];
         e.ld16 = F;
-        conv_to("conv_hr", P->cHB[2][2], H->hr, 4 * hh0, 4 * wp, F, e);
+        conv_plane("conv_hr", 2, 2, H->hr, 4 * hh0, 4 * wp, e);
       }
       final_planes(0, 2, 4 * hh0, 4 * wp);
       break;

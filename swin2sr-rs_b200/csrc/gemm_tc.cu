@@ -60,7 +60,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // most 24 KB for boxw <= 32) and three taps' weights
   constexpr int A_SLOT = PATCH ? 24576 : A_BYTES;
   constexpr int B_SLOT = PATCH ? 3 * B_BYTES : B_BYTES;
-  static_assert(!PATCH || (AR == 0 && STORE == STORE_PLANES), "patch mode: plane store only");
+  static_assert(!PATCH || (AR == 0 && (STORE == STORE_PLANES ||
+                                         (STORE == STORE_ROWS && WB == kWarpBufF16))),
+                "patch mode: the plane store, or fp16-only row stores");
   constexpr int F16OFF = WB >= kWarpBuf ? 8192 : 0;  // fp16 tiles within a warp's staging
   static_assert(WB == kWarpBuf || (WB == kWarpBufF16 && STORE == STORE_ROWS && RES != 2) ||
                     (WB == kStageFloats * 4 && STORE == STORE_SHUFFLE2) ||
@@ -649,9 +651,15 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   const bool ln = e.ln_n > 0;
   const int res = e.res_pre ? 1 : (e.res_post ? 2 : 0);
   const int store = e.store;
-  if (a.patch) {  // conv_last: kx patches, five slots (the plane store needs no staging)
+  if (a.patch) {  // 64-channel convs from kx patches
+    // conv_last: five slots (the plane store needs no staging)
     if (BN == 32 && act == ACT_NONE && !ln && res == 0 && store == STORE_PLANES)
       return launch_t<32, 5, ACT_NONE, false, 0, STORE_PLANES, 0, 0, true>(mapA, mapB, om, a, st);
+    // the nearest+conv head's 64 -> 64 convs (fp16 rows, LeakyReLU): three slots
+    if (BN == 64 && act == ACT_LRELU && !ln && res == 0 && store == STORE_ROWS && !e.o32 &&
+        !e.o32b)
+      return launch_t<64, 3, ACT_LRELU, false, 0, STORE_ROWS, 0, kWarpBufF16, true>(mapA, mapB, om,
+                                                                                  a, st);
     return cudaErrorNotSupported;
   }
   // embed 180 (Cp 192): QKV, convs, fc1, proj/fc2, patch_embed, stage tail, body skip
