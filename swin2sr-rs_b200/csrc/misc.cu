@@ -60,13 +60,19 @@ __global__ void __launch_bounds__(256) k_conv3_small(
     const float* __restrict__ in, const float* __restrict__ wgt, const float* __restrict__ bias,
     int B, int H, int W, int co_n, int act, float slope, float* __restrict__ o32, int ld32,
     __half* __restrict__ o16, int ld16) {
-  __shared__ float sw[kConvGroups * 8][27];
+  // weights of output channels (2p, 2p + 1) side by side: one float2 per tap feeds a
+  // packed two-channel fma
+  __shared__ float2 sw2[kConvGroups * 4][27];
   __shared__ float sb[kConvGroups * 8];
   const int lane = threadIdx.x, g = threadIdx.y;
   const int cbase = blockIdx.y * kConvGroups * 8;
   for (int i = g * 32 + lane; i < kConvGroups * 8 * 27; i += 256) {
-    const int co = cbase + i / 27;
-    sw[i / 27][i % 27] = co < co_n ? wgt[(size_t)co * 27 + i % 27] : 0.0f;
+    const int cl = i / 27, co = cbase + cl;
+    const float wv = co < co_n ? wgt[(size_t)co * 27 + i % 27] : 0.0f;
+    if (cl & 1)
+      sw2[cl >> 1][i % 27].y = wv;
+    else
+      sw2[cl >> 1][i % 27].x = wv;
   }
   for (int i = g * 32 + lane; i < kConvGroups * 8; i += 256)
     sb[i] = cbase + i < co_n ? bias[cbase + i] : 0.0f;
@@ -95,19 +101,28 @@ __global__ void __launch_bounds__(256) k_conv3_small(
                                         ? in[(((size_t)b * 3 + ci) * H + sy) * W + sx]
                                         : 0.0f;
         }
+    unsigned long long v2[27];  // each input twice: one operand for two channels
+#pragma unroll
+    for (int t = 0; t < 27; t++) v2[t] = f2_pack(v[t], v[t]);
     float acc[8];
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const float* wc = sw[g * 8 + j];
-      float a = sb[g * 8 + j];
+    for (int jp = 0; jp < 4; jp++) {
+      // channels 2jp, 2jp+1 of this warp: bias first, then ky, kx, ci, one fma each
+      const float2* wc = sw2[g * 4 + jp];
+      unsigned long long a2 = f2_pack(sb[g * 8 + 2 * jp], sb[g * 8 + 2 * jp + 1]);
 #pragma unroll
       for (int ky = 0; ky < 3; ky++)
 #pragma unroll
         for (int kx = 0; kx < 3; kx++)
 #pragma unroll
-          for (int ci = 0; ci < 3; ci++) a += wc[ci * 9 + ky * 3 + kx] * v[ci * 9 + ky * 3 + kx];
-      if (act == 2 && a < 0.0f) a *= slope;
-      acc[j] = a;
+          for (int ci = 0; ci < 3; ci++) {
+            const int t = ci * 9 + ky * 3 + kx;
+            const float2 w2 = wc[t];
+            a2 = f2_fma(f2_pack(w2.x, w2.y), v2[t], a2);
+          }
+      const float2 a = f2_unpack(a2);
+      acc[2 * jp] = (act == 2 && a.x < 0.0f) ? a.x * slope : a.x;
+      acc[2 * jp + 1] = (act == 2 && a.y < 0.0f) ? a.y * slope : a.y;
     }
     const size_t p = ((size_t)b * H + y) * W + x;
     const int nv = min(8, co_n - c0);
