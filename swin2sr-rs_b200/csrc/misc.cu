@@ -53,7 +53,8 @@ __global__ void k_pad_band(const float* __restrict__ x, float* __restrict__ y, i
 // 3x3 s1 p1 conv with 3 input channels, NCHW fp32 input -> NHWC outputs.
 // A warp is 32 consecutive pixels of one row and one group of 8 output channels:
 // the input loads coalesce across the warp, the weights are shared-memory
-// broadcasts, and each thread stores its pixel's 8 channels as 32 + 16 bytes.
+// broadcasts (two channels' weights per float2, feeding one packed f32x2 fma), and
+// each thread stores its pixel's 8 channels as 32 + 16 bytes.
 // Taps in the oracle's order: bias first, then ky, kx, ci.
 constexpr int kConvGroups = 8;  // channel groups per block (blockDim = 32 x 8)
 __global__ void __launch_bounds__(256) k_conv3_small(
