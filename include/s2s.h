@@ -31,7 +31,8 @@ enum {
   S2S_ERR_CUDA = 3,        /* any other CUDA error */
   S2S_ERR_NCCL = 4,        /* collective failure (sharded modes) */
   S2S_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up */
-  S2S_ERR_UNSUPPORTED = 6  /* architecture this build does not implement */
+  S2S_ERR_UNSUPPORTED = 6, /* architecture this build does not implement */
+  S2S_ERR_SELFTEST = 7     /* s2s_selftest: a consistency check failed (see its report) */
 };
 
 /* Reconstruction heads (src/weights.rs:18-29, Upsampler). */
@@ -253,6 +254,18 @@ int s2s_rgb8_device(int batch, int height, int width, const float* d_chw, int pn
  * format at [batch][hp][wp] (src/main.rs:395-418). Only bytes cross PCIe. */
 int s2s_forward_image(s2s_handle* h, int batch, int height, int width, const void* samples,
                       int channels, int bit_depth, int png_rows, uint8_t* out, uint8_t* aux);
+
+/* gpu::selftest (src/gpu.rs:889-1265; `--cuda-selftest`, src/main.rs:179-192): with the
+ * same arguments as s2s_create, build handles on `device` and check the fast paths
+ * against their plain forms on a seeded two-image batch of an odd size
+ * (2*window+3 x 3*window+5): the batch against each image alone (bitwise), a CUDA-graph
+ * replay against the eager forward (bitwise), the head convs from kx patches against
+ * nine tap boxes (1e-4) and the fused MLP against two GEMMs (2e-3, the parity
+ * tolerance: the two sum in different orders). One line per check
+ * ("<name> ok|FAILED max-abs <e> (tolerance <t>)") goes to `report` (NUL-terminated, at
+ * most `cap` bytes). Returns S2S_OK, S2S_ERR_SELFTEST, or the error that stopped it. */
+int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, int device,
+                 char* report, int cap);
 
 void s2s_destroy(s2s_handle* h);
 

@@ -15,9 +15,10 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libs2s.so"
 
 S2S_OK, S2S_ERR_OOM, S2S_ERR_INVALID, S2S_ERR_CUDA, S2S_ERR_NCCL, S2S_ERR_TIMEOUT, \
-    S2S_ERR_UNSUPPORTED = range(7)
+    S2S_ERR_UNSUPPORTED, S2S_ERR_SELFTEST = range(8)
 STATUS_NAMES = {0: "S2S_OK", 1: "S2S_ERR_OOM", 2: "S2S_ERR_INVALID", 3: "S2S_ERR_CUDA",
-                4: "S2S_ERR_NCCL", 5: "S2S_ERR_TIMEOUT", 6: "S2S_ERR_UNSUPPORTED"}
+                4: "S2S_ERR_NCCL", 5: "S2S_ERR_TIMEOUT", 6: "S2S_ERR_UNSUPPORTED",
+                7: "S2S_ERR_SELFTEST"}
 UPSAMPLER_CODE = {"pixelshuffle": 0, "pixelshuffledirect": 1, "nearest+conv": 2,
                   "pixelshuffle_aux": 3}
 
@@ -30,7 +31,7 @@ EXPORTS = ("s2s_create", "s2s_forward", "s2s_forward_batch", "s2s_forward_device
            "s2s_band_init_local", "s2s_band_rows", "s2s_forward_band", "s2s_forward_band_host",
            "s2s_band_partition", "s2s_band_halo_ops", "s2s_png_header", "s2s_png_decode",
            "s2s_png_encode_rgb8", "s2s_png_encode_rows", "s2s_free", "s2s_adjust_device",
-           "s2s_rgb8_device", "s2s_forward_image")
+           "s2s_rgb8_device", "s2s_forward_image", "s2s_selftest")
 BAND_ID_BYTES = 128
 
 
@@ -137,6 +138,9 @@ def load() -> ctypes.CDLL:
     L.s2s_forward_image.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_int, vp, vp]
     L.s2s_forward_image.restype = ctypes.c_int
+    L.s2s_selftest.argtypes = [ctypes.POINTER(S2SConfig), ctypes.POINTER(S2STensor), ctypes.c_int,
+                               ctypes.c_int, ctypes.c_char_p, ctypes.c_int]
+    L.s2s_selftest.restype = ctypes.c_int
     L.s2s_version.argtypes = []
     L.s2s_version.restype = ctypes.c_char_p
     _lib = L
@@ -160,25 +164,42 @@ def config_of(wt) -> S2SConfig:
     return cfg
 
 
+def tensor_array(wt):
+    """The s2s_tensor array of every tensor the architecture needs, and the numpy
+    buffers it borrows (keep them alive for the call)."""
+    names = wt.needed()
+    arr = (S2STensor * len(names))()
+    keep = []
+    for i, n in enumerate(names):
+        a = np.ascontiguousarray(wt.t(n), dtype=np.float32)
+        keep.append((n.encode(), a))
+        arr[i].name = keep[-1][0]
+        arr[i].data = _fp(a)
+        arr[i].ndim = a.ndim
+        for d in range(min(a.ndim, 4)):
+            arr[i].shape[d] = a.shape[d]
+    return arr, len(names), keep
+
+
+def selftest(wt, device: int = 0):
+    """s2s_selftest: (status, report) of the fast-path consistency checks."""
+    L = load()
+    arr, n, keep = tensor_array(wt)
+    buf = ctypes.create_string_buffer(4096)
+    rc = L.s2s_selftest(ctypes.byref(config_of(wt)), arr, n, device, buf, len(buf))
+    del keep
+    return rc, buf.value.decode()
+
+
 class Handle:
     """One s2s_handle on one device."""
 
     def __init__(self, wt, device: int = 0):
         L = load()
         self.L, self.wt, self.device = L, wt, device
-        names = wt.needed()
-        arr = (S2STensor * len(names))()
-        keep = []
-        for i, n in enumerate(names):
-            a = np.ascontiguousarray(wt.t(n), dtype=np.float32)
-            keep.append((n.encode(), a))
-            arr[i].name = keep[-1][0]
-            arr[i].data = _fp(a)
-            arr[i].ndim = a.ndim
-            for d in range(min(a.ndim, 4)):
-                arr[i].shape[d] = a.shape[d]
+        arr, n, keep = tensor_array(wt)
         h = ctypes.c_void_p()
-        rc = L.s2s_create(ctypes.byref(config_of(wt)), arr, len(names), device, ctypes.byref(h))
+        rc = L.s2s_create(ctypes.byref(config_of(wt)), arr, n, device, ctypes.byref(h))
         if rc != S2S_OK:
             raise S2SError(rc, L.s2s_last_error(None).decode())
         self.h = h

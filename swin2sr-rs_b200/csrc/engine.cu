@@ -18,6 +18,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -59,6 +60,13 @@ using namespace s2s;
 namespace {
 
 thread_local std::string g_create_error;
+
+// s2s_selftest creates its comparison handles with these settings of the validation
+// switches (-1: as the environment says).
+struct CreateFlags {
+  int unfused_mlp = -1, no_patch = -1;
+};
+thread_local CreateFlags g_create_flags;
 
 struct S2SError {
   int code;
@@ -1437,7 +1445,8 @@ int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, 
     g_create_error = "s2s_create: unsupported padded widths";
     return S2S_ERR_UNSUPPORTED;
   }
-  H->fused_mlp = (H->Cp == 192 && H->HIDp == 384) || (H->Cp == 64 && H->HIDp == 128);
+  const bool can_fuse = (H->Cp == 192 && H->HIDp == 384) || (H->Cp == 64 && H->HIDp == 128);
+  H->fused_mlp = can_fuse;
   {
     const char* f = getenv("S2S_UNFUSED_MLP");  // validation switch: the two-GEMM MLP path
     if (f && *f && strcmp(f, "0") != 0) H->fused_mlp = false;
@@ -1445,6 +1454,8 @@ int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, 
     H->no_patch = np && strcmp(np, "1") == 0;
     const char* g = getenv("S2S_GRAPHS");
     if (g && strcmp(g, "0") == 0) H->graphs = false;
+    if (g_create_flags.unfused_mlp >= 0) H->fused_mlp = can_fuse && g_create_flags.unfused_mlp == 0;
+    if (g_create_flags.no_patch >= 0) H->no_patch = g_create_flags.no_patch != 0;
   }
   TensorTable T;
   for (int i = 0; i < n_tensors; i++) T.t[tensors[i].name] = &tensors[i];
@@ -1752,6 +1763,92 @@ int s2s_forward_band_host(s2s_handle* H, int height, int width, const float* in,
     check_device_error(H);
     if (H->profiling) drain_profile(H);
   });
+}
+
+int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, int device,
+                 char* report, int cap) {
+  if (!cfg || !tensors) return S2S_ERR_INVALID;
+  std::string rep;
+  bool all_ok = true;
+  int status = S2S_OK;
+  s2s_handle* hs[3] = {nullptr, nullptr, nullptr};
+  auto check = [&](const char* name, double err, double tol) {
+    char b[192];
+    const bool ok = err <= tol;
+    snprintf(b, sizeof b, "%s %s max-abs %.3e (tolerance %.1e)\n", name, ok ? "ok" : "FAILED", err,
+             tol);
+    rep += b;
+    if (!ok) all_ok = false;
+  };
+  // handle k with the given validation switches; false (and the error in the report)
+  // when it cannot be made
+  auto make = [&](int k, int unfused_mlp, int no_patch) -> bool {
+    g_create_flags.unfused_mlp = unfused_mlp;
+    g_create_flags.no_patch = no_patch;
+    const int rc = s2s_create(cfg, tensors, n_tensors, device, &hs[k]);
+    g_create_flags = CreateFlags{};
+    if (rc != S2S_OK) {
+      rep += std::string("create failed: ") + s2s_last_error(nullptr) + "\n";
+      status = rc;
+      return false;
+    }
+    return true;
+  };
+  auto ran = [&](s2s_handle* h, int rc, const char* what) -> bool {
+    if (rc == S2S_OK) return true;
+    rep += std::string(what) + " failed: " + s2s_last_error(h) + "\n";
+    status = rc;
+    return false;
+  };
+  auto maxabs = [](const float* a, const float* b, size_t n) {
+    double m = 0.0;
+    for (size_t i = 0; i < n; i++) m = std::max(m, (double)std::fabs(a[i] - b[i]));
+    return m;
+  };
+  // two mean-adjusted images of an odd size (not a window multiple), fixed seed
+  const int win = cfg->window, sc = cfg->scale;
+  const int h = 2 * win + 3, w = 3 * win + 5, B = 2;
+  const size_t hw = (size_t)h * w, nin = 3 * hw, nout = (size_t)3 * h * sc * w * sc;
+  std::vector<float> in(B * nin), batch(B * nout), eager(nout), other(nout), replay(nout);
+  uint32_t st = 0x9E3779B9u;
+  for (int b = 0; b < B; b++)
+    for (int c = 0; c < 3; c++)
+      for (size_t i = 0; i < hw; i++) {
+        st = st * 1664525u + 1013904223u;
+        const float v = (float)(st >> 8) * (1.0f / 16777216.0f);
+        in[b * nin + c * hw + i] = (v - cfg->mean[c]) * cfg->img_range;
+      }
+  bool go = make(0, 0, 0);
+  // one call over the batch, then each image alone: the first alone runs eagerly, the
+  // second is captured as a graph, the third (image 0 again) replays it
+  go = go && ran(hs[0], s2s_forward_batch(hs[0], B, h, w, in.data(), batch.data(), nullptr),
+                 "batch forward");
+  go = go && ran(hs[0], s2s_forward(hs[0], h, w, in.data(), eager.data(), nullptr), "forward");
+  go = go && ran(hs[0], s2s_forward(hs[0], h, w, in.data() + nin, other.data(), nullptr),
+                 "forward");
+  go = go && ran(hs[0], s2s_forward(hs[0], h, w, in.data(), replay.data(), nullptr), "forward");
+  if (go) {
+    check("batch_vs_single", std::max(maxabs(batch.data(), eager.data(), nout),
+                                      maxabs(batch.data() + nout, other.data(), nout)), 0.0);
+    check("graph_replay_vs_eager", maxabs(replay.data(), eager.data(), nout), 0.0);
+  }
+  // the 64-channel head convs from tap boxes instead of kx patches
+  go = go && make(1, 0, 1) &&
+       ran(hs[1], s2s_forward(hs[1], h, w, in.data(), other.data(), nullptr), "forward");
+  if (go) check("patches_vs_tap_boxes", maxabs(other.data(), eager.data(), nout), 1e-4);
+  // the MLP as two GEMMs with the hidden activation in HBM
+  go = go && make(2, 1, 0) &&
+       ran(hs[2], s2s_forward(hs[2], h, w, in.data(), other.data(), nullptr), "forward");
+  if (go) check("fused_vs_unfused_mlp", maxabs(other.data(), eager.data(), nout), 2e-3);
+  for (s2s_handle*& x : hs)
+    if (x) s2s_destroy(x);
+  if (report && cap > 0) {
+    const size_t n = std::min(rep.size(), (size_t)cap - 1);
+    memcpy(report, rep.data(), n);
+    report[n] = 0;
+  }
+  if (status != S2S_OK) return status;
+  return all_ok ? S2S_OK : S2S_ERR_SELFTEST;
 }
 
 void s2s_destroy(s2s_handle* H) {

@@ -249,8 +249,8 @@ def test_conv_last_patches_match_the_tap_boxes(task, h, w, monkeypatch):
     ky taps) unless S2S_NO_PATCH=1 (read at create) asks for the nine tap boxes; the
     same fp16 operands summed in another tap order, so the outputs agree to fp32
     rounding."""
-    capi = importlib.import_module("swin2sr_b200.capi")
     P = pkg()
+    capi = importlib.import_module("swin2sr_b200.capi")
     wt = P.weights.Weights.seeded(task, 0, True)
     x = adjust(wt, np.random.default_rng(23).random((1, 3, h, w), dtype=np.float32))
     H = capi.Handle(wt)
@@ -304,3 +304,18 @@ def test_cpb_table_computed_on_device_from_the_mlp():
     # the two tables differ by the 512-term fp32 sums' order (measured 2.2e-4 at the
     # output on this case): within half the 2e-3 parity budget
     assert err <= 1e-3
+
+
+@pytest.mark.parametrize("task", ["classical_sr", "lightweight_sr", "real_sr", "compressed_sr"])
+def test_selftest_runs_every_consistency_check(task):
+    """s2s_selftest (the counterpart of the reference's --cuda-selftest) builds its own
+    handles and reports each fast path against its plain form."""
+    P = pkg()  # registers the package before its submodules are imported
+    capi = importlib.import_module("swin2sr_b200.capi")
+    wt = P.weights.Weights.seeded(task, 0, True)
+    rc, rep = capi.selftest(wt)
+    print(rep)
+    assert rc == capi.S2S_OK, rep
+    for name in ("batch_vs_single", "graph_replay_vs_eager", "patches_vs_tap_boxes",
+                 "fused_vs_unfused_mlp"):
+        assert f"{name} ok" in rep, rep
