@@ -192,3 +192,40 @@ def test_bench_kernel_accounting_adds_up_to_the_forward():
     assert f["mlp_fused"] == f["gemm_fc1"] + f["gemm_fc2"]
     T, Cp = hp * wp, 192
     assert bench.kernel_bytes(wt, 1, hp, wp)["mlp_fused"] == T * Cp * 12
+
+
+def test_bench_clock_sampler_reports_median_clock_and_throttle_reasons():
+    """The clocks record beside every bench number: median SM clock under load, the
+    maximum, and every throttle reason seen active in any sample."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("s2s_bench2", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+
+    class FakeProc:
+        def __init__(self, text):
+            self.text = text
+
+        def terminate(self):
+            pass
+
+        def communicate(self, timeout=None):
+            return self.text, ""
+
+    rows = [
+        "0, 1965, 1965, 700.1, 0x0, Not Active, Not Active, Not Active, Not Active",
+        "0, 1920, 1965, 980.0, 0x4, Not Active, Not Active, Not Active, Active",
+        "0, 1965, 1965, 990.5, 0x0, Not Active, Not Active, Not Active, Not Active",
+        "garbage line",
+        "0, [N/A], 1965, 1.0, 0x0, Not Active, Not Active, Not Active, Not Active",
+    ]
+    cs = bench.ClockSampler(0)
+    cs.proc = FakeProc("\n".join(rows))
+    rec = cs.stop()
+    assert rec == {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
+                   "samples": 3}
+    cs.proc = FakeProc("0, 1200, 1965, 500, 0x40, Active, Not Active, Active, Not Active\n")
+    rec = cs.stop()
+    assert rec["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"] and rec["sm_mhz"] == 1200.0
+    cs.proc = None
+    assert cs.stop() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
