@@ -282,6 +282,8 @@ Png parse_png(const uint8_t* d, size_t n, bool want_data) {
         default: ok = false;
       }
       if (!ok) fail(S2S_ERR_INVALID, "invalid PNG header");
+      // at most 2^34 pixels: with <= 8 bytes a pixel every size below fits 64 bits
+      if ((uint64_t)p.w * p.h > (1ull << 34)) fail(S2S_ERR_INVALID, "PNG dimensions too large");
       if (p.ctype == 3) fail(S2S_ERR_INVALID, "unsupported png colour type Indexed");
       p.channels = p.ctype == 0 ? 1 : p.ctype == 4 ? 2 : p.ctype == 2 ? 3 : 4;
       if (p.depth < 8) fail(S2S_ERR_INVALID, std::string("unsupported png bit depth ") + depth_name(p.depth));

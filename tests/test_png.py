@@ -437,3 +437,52 @@ def test_upscale_pngs_reports_device_errors_and_small_images():
         cli.upscale_pngs([_FakeHandle()], [pil_png(smooth_rgb(7, 16, 3), "RGB")])
     with pytest.raises(ValueError):
         cli.upscale_pngs([], pngs)
+
+
+def test_decoder_survives_corrupt_and_hostile_files():
+    """Random byte flips (with the CRCs recomputed, so the damage reaches inflate and
+    the unfilter), truncation at every chunk boundary and absurd dimensions end in
+    S2SError, never a crash or a read or write outside the buffers."""
+    C = capi()
+    rng = np.random.default_rng(31)
+    rows = rng.integers(0, 256, (13, 11 * 4), dtype=np.uint8)
+    base = spec_png(rows, 11, 13, 6, 8, 1, "random", rng)
+
+    def rechunk(data):  # recompute every chunk's CRC
+        out, off = bytearray(data[:8]), 8
+        while off + 12 <= len(data):
+            n = struct.unpack(">I", data[off:off + 4])[0]
+            if off + 12 + n > len(data):
+                break
+            body = data[off + 4:off + 8 + n]
+            out += data[off:off + 8 + n] + struct.pack(">I", zlib.crc32(body))
+            off += 12 + n
+        return bytes(out)
+
+    outcomes = {"ok": 0, "error": 0}
+    for _ in range(300):
+        b = bytearray(base)
+        for _ in range(int(rng.integers(1, 6))):
+            b[int(rng.integers(8, len(b)))] = int(rng.integers(0, 256))
+        try:
+            C.png_decode(rechunk(bytes(b)))
+            outcomes["ok"] += 1
+        except (C.S2SError, MemoryError, ValueError):
+            outcomes["error"] += 1
+    assert outcomes["error"] > 0
+    # a cut before the last IDAT chunk is complete loses image data (one after it, a
+    # missing IEND, decodes: the image is all there)
+    last_idat_end = base.rindex(b"IDAT") - 4 + 12 + struct.unpack(
+        ">I", base[base.rindex(b"IDAT") - 4:base.rindex(b"IDAT")])[0]
+    for cut in range(8, last_idat_end, 7):
+        with pytest.raises(C.S2SError):
+            C.png_decode(base[:cut])
+    assert np.array_equal(C.png_decode(base[:last_idat_end])[0].reshape(13, 44), rows)
+    for w, h in [(1 << 31 - 1, 1 << 31 - 1), (1 << 20, 1 << 20), (0, 5), (5, 0)]:
+        ihdr = struct.pack(">IIBBBBB", w, h, 8, 6, 0, 0, 0)
+        f = b"\x89PNG\r\n\x1a\n" + chunk(b"IHDR", ihdr) + chunk(b"IDAT", zlib.compress(b"\0" * 64)) \
+            + chunk(b"IEND", b"")
+        with pytest.raises(C.S2SError, match="too large|invalid PNG header"):
+            C.png_header(f)
+        L = C.load()
+        assert L.s2s_png_decode(f, len(f), None, 0) == C.S2S_ERR_INVALID
