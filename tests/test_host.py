@@ -229,3 +229,18 @@ def test_bench_clock_sampler_reports_median_clock_and_throttle_reasons():
     assert rec["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"] and rec["sm_mhz"] == 1200.0
     cs.proc = None
     assert cs.stop() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+
+def test_selftest_entry_point_reports_through_the_c_abi():
+    """s2s_selftest marshals the checkpoint like s2s_create and always fills its report:
+    here, with no device, the first handle cannot be made and it says so; on a GPU
+    machine it runs every check (tests/test_gpu_parity.py holds the GPU assertion)."""
+    import importlib
+    P = pkg()
+    C = importlib.import_module("swin2sr_b200.capi")
+    rc, rep = C.selftest(P.weights.Weights.seeded("lightweight_sr", 0))
+    assert rep.strip()
+    if rc == C.S2S_OK:
+        assert rep.count(" ok max-abs") == 4
+    else:
+        assert rc in (C.S2S_ERR_CUDA, C.S2S_ERR_UNSUPPORTED) and "create failed" in rep
