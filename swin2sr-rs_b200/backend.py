@@ -54,6 +54,13 @@ class Gpu(Backend):
         self.handle = capi.Handle(wt, device)
         self._aux = None
 
+    @classmethod
+    def from_handle(cls, handle):
+        """A backend over an existing handle (its weights are not uploaded again)."""
+        g = cls.__new__(cls)
+        g.wt, g.handle, g._aux = handle.wt, handle, None
+        return g
+
     def name(self) -> str:
         return "gpu"
 

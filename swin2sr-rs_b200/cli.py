@@ -1,7 +1,8 @@
 """Many PNG files through the device image path, batched and on several GPUs.
 
     python swin2sr-rs_b200/cli.py -m weights.safetensors -i a.png [b.png ...] -o OUT
-        [--devices 0,1,...] [--batch N] [--level L] [--threads T] [--aux OUT] [-q]
+        [--devices 0,1,...] [--batch N] [--level L] [--threads T] [--aux OUT]
+        [--tile N|auto] [--tile-pad P] [-q]
 
 The reference's CLI (src/main.rs:20-419) runs one image: load_rgb -> Pre::adjust
 -> forward -> to_rgb8 -> save_rgb. This driver runs that path for many images:
@@ -12,6 +13,13 @@ handle per device (data parallel, no communication), deflate of the filtered
 scanlines on the pool (s2s_png_encode_rows). Decode, forward and encode of
 different batches overlap. `-o` names a file for one input and a directory for
 several; `--aux` likewise, for the compressed_sr head (src/main.rs:380-418).
+
+`--tile` (src/main.rs:450-662) runs each image through the tiled driver instead:
+tiles of N pixels with `--tile-pad` of context (rounded up to a window multiple),
+halving the tile whenever the device runs out of memory. `auto` starts from one
+whole-image pass and relies on that retry. A tiled image takes the float path
+(backend.run_with_fallback), quantised and encoded on the host; the second image of
+`--aux` exists only for a whole-image pass, as in the reference.
 """
 from __future__ import annotations
 
@@ -125,6 +133,49 @@ def upscale_pngs(handles, pngs, batch: int = 8, level: int = -1, threads: int = 
     return out, aux
 
 
+def upscale_pngs_tiled(handles, pngs, tile: int, pad: int, level: int = -1, threads: int = 0,
+                       note=None, stats: dict | None = None):
+    """PNG bytes in -> PNG bytes out through the tiled driver, images spread over the
+    handles (one host thread each). Returns (outputs, the tile each image ran with)."""
+    from . import backend, image
+    if not handles:
+        raise ValueError("at least one handle")
+    wt = handles[0].wt
+    n = len(pngs)
+    out, ran = [None] * n, [None] * n
+    t0 = time.perf_counter()
+    headers = [capi.png_header(p) for p in pngs]
+    errors = []
+
+    def work(k):
+        gpu = backend.Gpu.from_handle(handles[k])
+        for i in range(k, n, len(handles)):
+            try:
+                samples, depth = capi.png_decode(pngs[i])
+                img = image.samples_to_image(samples, depth)
+                res, ran[i] = backend.run_with_fallback(wt, gpu, img.data, tile, pad, note)
+                rgb = image.Image(img.w * wt.scale, img.h * wt.scale, res).to_rgb8()
+                out[i] = capi.png_encode_rgb8(rgb, level, threads)
+            except Exception as e:  # noqa: BLE001 - reported after the join
+                errors.append(e)
+                return
+
+    ts = [threading.Thread(target=work, args=(k,)) for k in range(len(handles))]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    if errors:
+        raise errors[0]
+    if stats is not None:
+        s = wt.scale
+        stats["seconds"] = time.perf_counter() - t0
+        stats["images"] = n
+        stats["output_mpix"] = sum(h * s * w * s for w, h, _, _ in headers) / 1e6
+        stats["batches"] = n
+    return out, ran
+
+
 def main(argv=None) -> int:
     from . import weights as W
     ap = argparse.ArgumentParser(prog="swin2sr-b200", description=__doc__.split("\n\n")[0])
@@ -138,9 +189,27 @@ def main(argv=None) -> int:
     ap.add_argument("--batch", type=int, default=8, help="images of one size per forward")
     ap.add_argument("--level", type=int, default=-1, help="zlib level -1..9")
     ap.add_argument("--threads", type=int, default=0, help="host threads (0 = all cores)")
+    ap.add_argument("--tile", default="0",
+                    help="tile side in pixels, 0 for one whole-image pass (the only exact "
+                         "mode), or auto: whole image, halved on out-of-memory")
+    ap.add_argument("--tile-pad", type=int, default=32,
+                    help="context kept around each tile (rounded up to a window multiple)")
     ap.add_argument("-q", "--quiet", action="store_true")
     a = ap.parse_args(argv)
+    if a.tile == "auto":
+        tile = 0
+    else:
+        try:
+            tile = int(a.tile)
+        except ValueError:
+            print("error: --tile takes a number or `auto`", file=sys.stderr)
+            return 1
+    tiled = a.tile != "0"
     wt = W.Weights.load(a.model)
+    if a.aux and tiled:
+        print(f"error: --aux: the second image exists only for a single pass, and --tile "
+              f"{a.tile} would tile it. Re-run with --tile 0.", file=sys.stderr)
+        return 1
     if a.aux and wt.upsampler != "pixelshuffle_aux":
         print(f"error: --aux: the {wt.upsampler} head has one output; only the compressed_sr "
               f"head (pixelshuffle_aux) produces a second image", file=sys.stderr)
@@ -160,8 +229,15 @@ def main(argv=None) -> int:
     handles = [capi.Handle(wt, int(d)) for d in a.devices.split(",")]
     try:
         stats: dict = {}
-        outs, auxs = upscale_pngs(handles, pngs, a.batch, a.level, a.threads, bool(a.aux), stats)
-    except capi.S2SError as e:
+        if tiled:
+            note = None if a.quiet else (lambda m: print(f"  {m}", file=sys.stderr))
+            outs, _ = upscale_pngs_tiled(handles, pngs, tile, a.tile_pad, a.level, a.threads,
+                                         note, stats)
+            auxs = [None] * len(outs)
+        else:
+            outs, auxs = upscale_pngs(handles, pngs, a.batch, a.level, a.threads, bool(a.aux),
+                                      stats)
+    except (capi.S2SError, RuntimeError) as e:
         print(f"error: {e}", file=sys.stderr)
         return 1
     finally:

@@ -486,3 +486,65 @@ def test_decoder_survives_corrupt_and_hostile_files():
             C.png_header(f)
         L = C.load()
         assert L.s2s_png_decode(f, len(f), None, 0) == C.S2S_ERR_INVALID
+
+
+class _FakeFloatHandle:
+    """Stands in for capi.Handle in the tiled path: forward_batch undoes the mean
+    adjustment and repeats each pixel `scale` times (a local operation, so every
+    tiling gives the whole-image result); it runs out of memory above `limit` pixels."""
+
+    def __init__(self, wt, limit=None):
+        self.wt, self.limit, self.sizes = wt, limit, []
+
+    def forward_batch(self, x):
+        B, _, h, w = x.shape
+        self.sizes.append((h, w))
+        if self.limit is not None and h * w > self.limit:
+            capi_mod = cli_mod().capi
+            raise capi_mod.S2SError(capi_mod.S2S_ERR_OOM,
+                                    "cudaMalloc: CUDA_ERROR_OUT_OF_MEMORY (fake)")
+        m = np.asarray(self.wt.mean, np.float32).reshape(1, 3, 1, 1)
+        img = x / np.float32(self.wt.img_range) + m
+        s = self.wt.scale
+        return img.repeat(s, axis=2).repeat(s, axis=3), None
+
+    def workspace_bytes(self, B, h, w):
+        return B * h * w * 1000
+
+
+def test_tiled_cli_path_matches_the_whole_image_and_recovers_from_oom():
+    cli = cli_mod()
+    P = pkg()
+    wt = P.weights.Weights.seeded("classical_sr", 0)
+    imgs = [smooth_rgb(40, 56, 1), smooth_rgb(33, 20, 2)]
+    pngs = [pil_png(a, "RGB") for a in imgs]
+    want = [np.array(a).repeat(4, axis=0).repeat(4, axis=1) for a in imgs]
+    for tile in (16, 0):
+        outs, ran = cli.upscale_pngs_tiled([_FakeFloatHandle(wt), _FakeFloatHandle(wt)], pngs,
+                                           tile, 8)
+        assert ran == [tile, tile]
+        for o, w_ in zip(outs, want):
+            assert np.array_equal(np.array(PILImage.open(io.BytesIO(o))), w_)
+    notes = []
+    h = _FakeFloatHandle(wt, limit=40 * 40)
+    outs, ran = cli.upscale_pngs_tiled([h], pngs[:1], 0, 8, note=notes.append)
+    # 40x56 (2240 px) is over the limit; half the long side, a 24-pixel tile with 8 of
+    # context, makes crops of at most 40x40 = 1600 px, which fit
+    assert ran == [24] and len(notes) == 1 and "retrying with a 24x24 tile" in notes[0]
+    assert np.array_equal(np.array(PILImage.open(io.BytesIO(outs[0]))), want[0])
+    assert max(a * b for a, b in h.sizes[1:]) <= 40 * 40
+
+
+def test_cli_refuses_aux_with_tiling(tmp_path, capsys):
+    cli = cli_mod()
+    P = pkg()
+    wt = P.weights.Weights.seeded("compressed_sr", 0)
+    ck = tmp_path / "cx.safetensors"
+    P.weights.save_safetensors(str(ck), wt.tensors, wt.meta)
+    src = tmp_path / "in.png"
+    src.write_bytes(pil_png(smooth_rgb(16, 16, 1), "RGB"))
+    rc = cli.main(["-m", str(ck), "-i", str(src), "-o", str(tmp_path / "o.png"), "--aux",
+                   str(tmp_path / "a.png"), "--tile", "64", "-q"])
+    assert rc == 1 and "only for a single pass" in capsys.readouterr().err
+    rc = cli.main(["-m", str(ck), "-i", str(src), "-o", str(tmp_path / "o.png"), "--tile", "x"])
+    assert rc == 1 and "--tile takes a number" in capsys.readouterr().err
