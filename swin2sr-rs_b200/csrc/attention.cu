@@ -24,6 +24,12 @@
 // pad lanes zero) are gathered with one bulk copy per token row into a padded,
 // bank-conflict-free shared-memory layout, and outputs are scattered back to the
 // same rows.
+//
+// SPLIT (two-term operands, the 60-wide network): every QKV row carries a second
+// fp16 term lo = fp16(x - hi) `lo_q` halves after the first, gathered beside it;
+//   S = Qhi Khi^T + Qlo Khi^T + Qhi Klo^T,   O = P Vhi + P Vlo
+// and the output is written as hi and lo terms too (lo `lo_out` halves after hi).
+// The dot products then carry about 21 bits of the operands instead of 11.
 #include "common.cuh"
 
 namespace s2s {
@@ -77,16 +83,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
-// DP: padded head dim (16 or 32); HPC heads per CTA. Window of 64 tokens (win = 8).
-template <int DP, int HPC>
-__global__ void __launch_bounds__(128 * HPC + 32, HPC == 1 ? 5 : 1) k_window_attention(
+// DP: padded head dim (16 or 32); HPC heads per CTA; SPLIT: two-term operands.
+// Window of 64 tokens (win = 8). row_h: halves per QKV token row.
+template <int DP, int HPC, bool SPLIT>
+__global__ void __launch_bounds__(128 * HPC + 32, SPLIT ? 3 : (HPC == 1 ? 5 : 1)) k_window_attention(
     const __half* __restrict__ qkv, __half* __restrict__ out, const float* __restrict__ cpb,
-    const int* __restrict__ rows, int heads, int hd, int ld_out,
+    const int* __restrict__ rows, int heads, int hd, int ld_out, int row_h, int lo_q, int lo_out,
     int nwh, int nww, int hp, int wp, int shift, int nwin_total, int wh_off) {
   constexpr int N = 64;
   constexpr int NS = N;                        // bias row (floats), XOR-swizzled by row % 8
   constexpr int SEG = HPC * 3 * DP;            // halves of this CTA's heads per token row
-  constexpr int SSTRIDE = SEG + 8;             // padded smem row: odd number of 16 B units
+  constexpr int SROW = SPLIT ? 2 * SEG : SEG;  // with the lo terms after the hi terms
+  constexpr int SSTRIDE = SROW + 8;            // padded smem row: odd number of 16 B units
+  static_assert(((SSTRIDE * 2 / 16) & 1) == 1, "bank-conflict-free row stride");
   constexpr int CW = 4 * HPC;                  // compute warps
   extern __shared__ uint8_t smem_raw[];
   float* scpb = reinterpret_cast<float*>(smem_raw);                       // [HPC][64][NS]
@@ -100,7 +109,6 @@ __global__ void __launch_bounds__(128 * HPC + 32, HPC == 1 ? 5 : 1) k_window_att
   const int wstep = gridDim.x / NG;           // host launches a multiple of NG CTAs
   const int nw = nwh * nww;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row_h = 3 * heads * DP;            // halves per full QKV token row
   const int win0 = blockIdx.x / NG;
 
   if (threadIdx.x == 0) {
@@ -128,12 +136,17 @@ __global__ void __launch_bounds__(128 * HPC + 32, HPC == 1 ? 5 : 1) k_window_att
       // rows of this window (loaded before waiting, so their latency overlaps the wait)
       const int r0 = rows[(size_t)win * N + lane], r1 = rows[(size_t)win * N + 32 + lane];
       if (i >= 2 && !mbar_wait(&empty[b], ((i >> 1) - 1) & 1, DEV_TIMEOUT_EMPTY)) break;
-      if (lane == 0) mbar_arrive_expect_tx(&full[b], (uint32_t)(N * SEG * 2));
+      if (lane == 0) mbar_arrive_expect_tx(&full[b], (uint32_t)(N * SROW * 2));
       __syncwarp();
       __half* dst = sqb + (size_t)b * N * SSTRIDE;
-      bulk_g2s(dst + (size_t)lane * SSTRIDE, qkv + (size_t)r0 * row_h + h0 * 3 * DP, SEG * 2, &full[b]);
-      bulk_g2s(dst + (size_t)(32 + lane) * SSTRIDE, qkv + (size_t)r1 * row_h + h0 * 3 * DP, SEG * 2,
-               &full[b]);
+      const __half* s0 = qkv + (size_t)r0 * row_h + h0 * 3 * DP;
+      const __half* s1 = qkv + (size_t)r1 * row_h + h0 * 3 * DP;
+      bulk_g2s(dst + (size_t)lane * SSTRIDE, s0, SEG * 2, &full[b]);
+      bulk_g2s(dst + (size_t)(32 + lane) * SSTRIDE, s1, SEG * 2, &full[b]);
+      if constexpr (SPLIT) {
+        bulk_g2s(dst + (size_t)lane * SSTRIDE + SEG, s0 + lo_q, SEG * 2, &full[b]);
+        bulk_g2s(dst + (size_t)(32 + lane) * SSTRIDE + SEG, s1 + lo_q, SEG * 2, &full[b]);
+      }
     }
     return;
   }
@@ -187,10 +200,11 @@ __global__ void __launch_bounds__(128 * HPC + 32, HPC == 1 ? 5 : 1) k_window_att
     for (int j = 0; j < 8; j++) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
 #pragma unroll
     for (int kk = 0; kk < DP / 16; kk++) {
-      uint32_t a0, a1, a2, a3;
+      uint32_t a0, a1, a2, a3, l0 = 0, l1 = 0, l2 = 0, l3 = 0;
       const int arow = rb * 16 + (lane & 15);
       const int acol = qoff + kk * 16 + (lane >> 4) * 8;
       ldsm_x4(sbase + (uint32_t)((arow * SSTRIDE + acol) * 2), a0, a1, a2, a3);
+      if constexpr (SPLIT) ldsm_x4(sbase + (uint32_t)((arow * SSTRIDE + acol + SEG) * 2), l0, l1, l2, l3);
 #pragma unroll
       for (int j = 0; j < 8; j += 2) {
         uint32_t b0, b1, b2, b3;
@@ -199,6 +213,13 @@ __global__ void __launch_bounds__(128 * HPC + 32, HPC == 1 ? 5 : 1) k_window_att
         ldsm_x4(sbase + (uint32_t)((krow * SSTRIDE + kcol) * 2), b0, b1, b2, b3);
         mma16816(sacc[j], a0, a1, a2, a3, b0, b1);
         mma16816(sacc[j + 1], a0, a1, a2, a3, b2, b3);
+        if constexpr (SPLIT) {
+          mma16816(sacc[j], l0, l1, l2, l3, b0, b1);
+          mma16816(sacc[j + 1], l0, l1, l2, l3, b2, b3);
+          ldsm_x4(sbase + (uint32_t)((krow * SSTRIDE + kcol + SEG) * 2), b0, b1, b2, b3);
+          mma16816(sacc[j], a0, a1, a2, a3, b0, b1);
+          mma16816(sacc[j + 1], a0, a1, a2, a3, b2, b3);
+        }
       }
     }
 
@@ -268,6 +289,11 @@ __global__ void __launch_bounds__(128 * HPC + 32, HPC == 1 ? 5 : 1) k_window_att
         ldsm_x4_t(sbase + (uint32_t)((vrow * SSTRIDE + vcol) * 2), b0, b1, b2, b3);
         mma16816(oacc[n], a0, a1, a2, a3, b0, b1);
         mma16816(oacc[n + 1], a0, a1, a2, a3, b2, b3);
+        if constexpr (SPLIT) {
+          ldsm_x4_t(sbase + (uint32_t)((vrow * SSTRIDE + vcol + SEG) * 2), b0, b1, b2, b3);
+          mma16816(oacc[n], a0, a1, a2, a3, b0, b1);
+          mma16816(oacc[n + 1], a0, a1, a2, a3, b2, b3);
+        }
       }
     }
     // this warp is done with the buffer
@@ -280,67 +306,70 @@ __global__ void __launch_bounds__(128 * HPC + 32, HPC == 1 ? 5 : 1) k_window_att
     for (int n = 0; n < DP / 8; n++) {
       const int d = n * 8 + 2 * t4;
       if (d < hd) {
-        *reinterpret_cast<__half2*>(o0 + d) =
-            __floats2half2_rn(oacc[n][0] * inv0, oacc[n][1] * inv0);
-        *reinterpret_cast<__half2*>(o1 + d) =
-            __floats2half2_rn(oacc[n][2] * inv1, oacc[n][3] * inv1);
+        const float v00 = oacc[n][0] * inv0, v01 = oacc[n][1] * inv0;
+        const float v10 = oacc[n][2] * inv1, v11 = oacc[n][3] * inv1;
+        const __half2 h0 = __floats2half2_rn(v00, v01), h1 = __floats2half2_rn(v10, v11);
+        *reinterpret_cast<__half2*>(o0 + d) = h0;
+        *reinterpret_cast<__half2*>(o1 + d) = h1;
+        if constexpr (SPLIT) {
+          const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+          *reinterpret_cast<__half2*>(o0 + lo_out + d) = __floats2half2_rn(v00 - f0.x, v01 - f0.y);
+          *reinterpret_cast<__half2*>(o1 + lo_out + d) = __floats2half2_rn(v10 - f1.x, v11 - f1.y);
+        }
       }
     }
   }
 }
 
-template <int DP, int HPC>
-cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb,
-                          const int* rows, int nwin_total, int heads, int hd, int ld_out, int nwh,
-                          int nww, int hp, int wp, int shift, int wh_off, cudaStream_t st) {
-  constexpr int SEG = HPC * 3 * DP;
-  const size_t smem = (size_t)HPC * 64 * 64 * 4 + (size_t)2 * 64 * (SEG + 8) * 2 + 5 * 8 + 16;
-  static int ctas = 0;  // resident CTAs per device
-  if (ctas == 0) {
-    cudaError_t err = cudaFuncSetAttribute(k_window_attention<DP, HPC>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (err != cudaSuccess) return err;
-    int dev = 0, sms = 0, occ = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_window_attention<DP, HPC>,
-                                                        128 * HPC + 32, smem);
-    if (err != cudaSuccess) return err;
-    if (occ < 1) return cudaErrorInvalidConfiguration;
-    ctas = sms * occ;
-  }
+template <int DP, bool SPLIT>
+cudaError_t launch_attn_t(const __half* qkv, __half* out, const float* cpb, const int* rows,
+                          int nwin_total, int heads, int hd, int ld_out, int row_h, int lo_q,
+                          int lo_out, int nwh, int nww, int hp, int wp, int shift, int wh_off,
+                          cudaStream_t st) {
+  constexpr int HPC = 1;
+  constexpr int SEG = HPC * 3 * DP, SROW = SPLIT ? 2 * SEG : SEG;
+  const size_t smem = (size_t)HPC * 64 * 64 * 4 + (size_t)2 * 64 * (SROW + 8) * 2 + 5 * 8 + 16;
+  static LaunchSetup setup;  // resident CTAs, per device
+  int ctas = 0;
+  const cudaError_t err =
+      resident_ctas(setup, k_window_attention<DP, HPC, SPLIT>, 128 * HPC + 32, smem, &ctas);
+  if (err != cudaSuccess) return err;
   const int NG = heads / HPC;
   long G = (long)nwin_total * NG;
   if (G > ctas) G = ctas;
   G = (G / NG) * NG;
   if (G < NG) G = NG;
-  return launch_pdl(k_window_attention<DP, HPC>, dim3((unsigned)G), dim3(128 * HPC + 32), smem, st,
-                    qkv, out, cpb, rows, heads, hd, ld_out, nwh, nww, hp, wp, shift, nwin_total,
-                    wh_off);
+  return launch_pdl(k_window_attention<DP, HPC, SPLIT>, dim3((unsigned)G), dim3(128 * HPC + 32),
+                    smem, st, qkv, out, cpb, rows, heads, hd, ld_out, row_h, lo_q, lo_out, nwh,
+                    nww, hp, wp, shift, nwin_total, wh_off);
 }
 
 }  // namespace
 
+// One head per CTA: the smallest CTA (about 43 KB of shared memory), so five fit on an
+// SM and their window streams hide each other's latency (two heads per CTA, two CTAs
+// per SM, measured 11 % slower). row_h: halves per QKV token row; split: the rows
+// carry lo terms lo_q halves after the hi terms, and the output gets its lo terms
+// lo_out halves after hi.
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
-                                    const int* rows, int nwin_total,
-                                    int heads, int hd, int dp, int ld_out, int nwh, int nww,
-                                    int hp, int wp, int shift, int wh_off, cudaStream_t st) {
-  // one head per CTA: the smallest CTA (about 43 KB of shared memory), so five fit on
-  // an SM and their window streams hide each other's latency (two heads per CTA, two
-  // CTAs per SM, measured 11 % slower)
-  const bool pair = false;
-  if (dp == 32 && pair)
-    return launch_attn_t<32, 2>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, wh_off, st);
+                                    const int* rows, int nwin_total, int heads, int hd, int dp,
+                                    int ld_out, int row_h, int split, int lo_q, int lo_out,
+                                    int nwh, int nww, int hp, int wp, int shift, int wh_off,
+                                    cudaStream_t st) {
+  if (row_h < 3 * heads * dp || (split && (lo_q < 3 * heads * dp || row_h < lo_q + 3 * heads * dp)))
+    return cudaErrorInvalidValue;
+  if (dp == 32 && !split)
+    return launch_attn_t<32, false>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, row_h, 0,
+                                    0, nwh, nww, hp, wp, shift, wh_off, st);
   if (dp == 32)
-    return launch_attn_t<32, 1>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, wh_off, st);
-  if (dp == 16 && pair)
-    return launch_attn_t<16, 2>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, wh_off, st);
+    return launch_attn_t<32, true>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, row_h, lo_q,
+                                   lo_out, nwh, nww, hp, wp, shift, wh_off, st);
+  if (dp == 16 && !split)
+    return launch_attn_t<16, false>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, row_h, 0,
+                                    0, nwh, nww, hp, wp, shift, wh_off, st);
   if (dp == 16)
-    return launch_attn_t<16, 1>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, nwh,
-                                nww, hp, wp, shift, wh_off, st);
+    return launch_attn_t<16, true>(qkv, out, cpb, rows, nwin_total, heads, hd, ld_out, row_h, lo_q,
+                                   lo_out, nwh, nww, hp, wp, shift, wh_off, st);
   return cudaErrorInvalidValue;
 }
 

@@ -12,8 +12,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <utility>
 
 namespace s2s {
@@ -54,6 +56,43 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Launch set-up of one kernel, per device: its dynamic shared-memory limit is raised
+// and the CTAs that fit on the device at once are counted the first time the kernel
+// is launched on that device (with it current); later launches read the count.
+// Thread-safe: handles on several devices may launch from several host threads.
+constexpr int kMaxDevices = 64;
+struct LaunchSetup {
+  std::mutex mu;
+  std::atomic<int> ctas[kMaxDevices] = {};
+};
+
+template <typename Kern>
+cudaError_t resident_ctas(LaunchSetup& ls, Kern kernel, int threads, size_t smem, int* ctas) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  int n = ls.ctas[dev].load(std::memory_order_acquire);
+  if (n == 0) {
+    std::lock_guard<std::mutex> lock(ls.mu);
+    n = ls.ctas[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
+      err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (err != cudaSuccess) return err;
+      int sms = 0, occ = 0;
+      err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (err != cudaSuccess) return err;
+      err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem);
+      if (err != cudaSuccess) return err;
+      if (occ < 1) return cudaErrorInvalidConfiguration;
+      n = sms * occ;
+      ls.ctas[dev].store(n, std::memory_order_release);
+    }
+  }
+  *ctas = n;
+  return cudaSuccess;
 }
 
 // Error codes recorded on the device (first error wins).

@@ -36,16 +36,17 @@
 
 namespace s2s {
 cudaError_t launch_window_attention(const __half* qkv, __half* out, const float* cpb,
-                                    const int* rows, int nwin_total,
-                                    int heads, int hd, int dp, int ld_out, int nwh, int nww,
-                                    int hp, int wp, int shift, int wh_off, cudaStream_t st);
+                                    const int* rows, int nwin_total, int heads, int hd, int dp,
+                                    int ld_out, int row_h, int split, int lo_q, int lo_out,
+                                    int nwh, int nww, int hp, int wp, int shift, int wh_off,
+                                    cudaStream_t st);
 cudaError_t launch_pad_reflect(const float* x, float* y, int B, int c, int h, int w, int hp,
                                int wp, cudaStream_t st);
 cudaError_t launch_pad_band(const float* x, float* y, int c, int h, int w, int hp, int wp, int rows,
                             int y0, cudaStream_t st);
 cudaError_t launch_conv3_small(const float* in, const float* wgt, const float* bias, int B, int H,
                                int W, int co_n, int act, float slope, float* o32, int ld32,
-                               __half* o16, int ld16, cudaStream_t st);
+                               __half* o16, int ld16, int lo16, cudaStream_t st);
 cudaError_t launch_zero_cols_f16(__half* x, size_t rows, int c0, int ld, cudaStream_t st);
 cudaError_t launch_bicubic(const float* in, float* out, int BC, int h, int w, int oh, int ow,
                            cudaStream_t st);
@@ -64,7 +65,7 @@ thread_local std::string g_create_error;
 // s2s_selftest creates its comparison handles with these settings of the validation
 // switches (-1: as the environment says).
 struct CreateFlags {
-  int unfused_mlp = -1, no_patch = -1;
+  int unfused_mlp = -1, no_patch = -1, split = -1;
 };
 thread_local CreateFlags g_create_flags;
 
@@ -158,6 +159,15 @@ struct s2s_handle {
   int device = 0;
   s2s_config cfg;
   int C = 0, Cp = 0, heads = 0, hd = 0, DP = 0, NQ = 0, HIDp = 0, feat = 64;
+  // Two-term operands (split): every fp16 tensor-core operand of the body carries
+  // hi = fp16(x) and lo = fp16(x - hi) side by side in its row ([hi | lo]), and the
+  // weights [W_hi | W_hi | W_lo] along K, so one tcgen05 accumulation over three K
+  // blocks is hi*W_hi + lo*W_hi + hi*W_lo: about 21 bits of each operand instead of
+  // 11. The 60-wide network needs it for the 2e-3 parity bound (with single fp16
+  // operands its output moves by up to 5e-3); the 180-wide ones do not (<= 7e-4).
+  // Cs, NQs, HIDs: row strides (halves) of the X16/AO/F0h, QKV and H16 buffers.
+  bool split = false;
+  int Cs = 0, NQs = 0, HIDs = 0;
   float* cf_w = nullptr;
   float* cf_b = nullptr;
   TcWeight pe;
@@ -180,7 +190,7 @@ struct s2s_handle {
   std::vector<ProfEntry> prof_pending;
   std::vector<cudaEvent_t> ev_pool;
   std::map<std::string, std::pair<long, double>> prof;
-  long long launches = 0;
+  std::atomic<long long> launches{0};  // kernels launched (all calls on the handle)
   bool fused_mlp = false;      // (Cp, HIDp) has a fused MLP kernel
   bool graphs = true;          // replay repeated forwards as CUDA graphs (S2S_GRAPHS=0: off)
   bool no_patch = false;       // conv_last from nine tap boxes (S2S_NO_PATCH=1: validation)
@@ -235,24 +245,40 @@ void finish_tc(s2s_handle* H, TcWeight& tw, const std::vector<__half>& w, const 
     fail(S2S_ERR_CUDA, "cuTensorMapEncodeTiled failed for a weight operand");
 }
 
-// Linear [n_out][n_in] -> fp16 [N][K] with row remap (dst row -> src row or -1).
+// Store weight value v at K block position k of a row of `kb` values: one fp16 term,
+// or, two-term, [hi | hi | lo] over three K blocks (the A operand's [hi | lo] row is
+// read as hi, lo, hi against them).
+inline void put_w(__half* row, int k, int kb, float v, bool split) {
+  const __half hi = __float2half_rn(v);
+  row[k] = hi;
+  if (split) {
+    row[kb + k] = hi;
+    row[2 * kb + k] = __float2half_rn(v - __half2float(hi));
+  }
+}
+
+// Linear [n_out][n_in] -> fp16 [N][K] with row remap (dst row -> src row or -1);
+// two-term: [N][3K].
 void pack_linear(s2s_handle* H, TcWeight& tw, const float* W, const float* bias, int n_in, int N,
-                 int K, int BN, const std::vector<int>& rowmap) {
-  std::vector<__half> w((size_t)N * K, __float2half(0.0f));
+                 int K, int BN, const std::vector<int>& rowmap, bool split = false) {
+  const int KK = split ? 3 * K : K;
+  std::vector<__half> w((size_t)N * KK, __float2half(0.0f));
   std::vector<float> b(N, 0.0f);
   for (int r = 0; r < N; r++) {
     const int s = rowmap[r];
     if (s < 0) continue;
-    for (int k = 0; k < n_in; k++) w[(size_t)r * K + k] = __float2half_rn(W[(size_t)s * n_in + k]);
+    for (int k = 0; k < n_in; k++) put_w(&w[(size_t)r * KK], k, K, W[(size_t)s * n_in + k], split);
     if (bias) b[r] = bias[s];
   }
-  finish_tc(H, tw, w, b, N, K, BN);
+  finish_tc(H, tw, w, b, N, KK, BN);
 }
 
-// Conv3x3 [co][ci][3][3] -> fp16 [N][9*Cip], K index = (ky*3+kx)*Cip + c.
+// Conv3x3 [co][ci][3][3] -> fp16 [N][9*Cip], K index = (ky*3+kx)*Cip + c; two-term:
+// [N][9*3*Cip], each tap's block [hi | hi | lo].
 void pack_conv(s2s_handle* H, TcWeight& tw, const float* W, const float* bias, int ci, int Cip,
-               int N, int BN, const std::vector<int>& rowmap) {
-  const int K = 9 * Cip;
+               int N, int BN, const std::vector<int>& rowmap, bool split = false) {
+  const int TB = split ? 3 * Cip : Cip;  // K per tap
+  const int K = 9 * TB;
   std::vector<__half> w((size_t)N * K, __float2half(0.0f));
   std::vector<float> b(N, 0.0f);
   for (int r = 0; r < N; r++) {
@@ -260,7 +286,7 @@ void pack_conv(s2s_handle* H, TcWeight& tw, const float* W, const float* bias, i
     if (s < 0) continue;
     for (int c = 0; c < ci; c++)
       for (int t = 0; t < 9; t++)
-        w[(size_t)r * K + t * Cip + c] = __float2half_rn(W[((size_t)s * ci + c) * 9 + t]);
+        put_w(&w[(size_t)r * K + t * TB], c, Cip, W[((size_t)s * ci + c) * 9 + t], split);
     b[r] = bias[s];
   }
   finish_tc(H, tw, w, b, N, K, BN);
@@ -338,18 +364,19 @@ void build_weights(s2s_handle* H, const TensorTable& T, std::vector<void*>& tmp)
   const int C = c.embed, Cp = H->Cp, hd = H->hd, DP = H->DP, heads = H->heads;
   const int HID = c.mlp_ratio * C, HIDp = H->HIDp;
   const int n = c.window * c.window;
+  const bool sp = H->split;
   // top
   H->cf_w = upload(H, std::vector<float>(T.get("conv_first.weight", (int64_t)C * 27),
                                          T.get("conv_first.weight") + (size_t)C * 27));
   H->cf_b = upload(H, std::vector<float>(T.get("conv_first.bias", C), T.get("conv_first.bias") + C));
   pack_linear(H, H->pe, T.get("patch_embed.proj.weight", (int64_t)C * C),
-              T.get("patch_embed.proj.bias", C), C, Cp, Cp, Cp, identity_rows(Cp, C));
+              T.get("patch_embed.proj.bias", C), C, Cp, Cp, Cp, identity_rows(Cp, C), sp);
   H->pe_g = upload(H, padded(T.get("patch_embed.norm.weight", C), C, Cp));
   H->pe_b = upload(H, padded(T.get("patch_embed.norm.bias", C), C, Cp));
   H->nrm_g = upload(H, padded(T.get("norm.weight", C), C, Cp));
   H->nrm_b = upload(H, padded(T.get("norm.bias", C), C, Cp));
   pack_conv(H, H->cab, T.get("conv_after_body.weight", (int64_t)C * C * 9),
-            T.get("conv_after_body.bias", C), C, Cp, Cp, Cp, identity_rows(Cp, C));
+            T.get("conv_after_body.bias", C), C, Cp, Cp, Cp, identity_rows(Cp, C), sp);
   // stages
   H->stages.resize(c.n_depths);
   std::vector<float> zeros(C, 0.0f);
@@ -380,16 +407,17 @@ void build_weights(s2s_handle* H, const TensorTable& T, std::vector<void*>& tmp)
       for (int part = 0; part < 3; part++)
         for (int h = 0; h < heads; h++)
           for (int d = 0; d < hd; d++) qmap[(h * 3 + part) * DP + d] = part * C + h * hd + d;
-      pack_linear(H, bl.qkv, W3.data(), b3.data(), C, H->NQ, Cp, n_tile_for(H->NQ), qmap);
+      pack_linear(H, bl.qkv, W3.data(), b3.data(), C, H->NQ, Cp, n_tile_for(H->NQ), qmap, sp);
       pack_linear(H, bl.proj, T.get(p + "attn.proj.weight", (int64_t)C * C),
-                  T.get(p + "attn.proj.bias", C), C, Cp, Cp, Cp, identity_rows(Cp, C));
+                  T.get(p + "attn.proj.bias", C), C, Cp, Cp, Cp, identity_rows(Cp, C), sp);
       pack_linear(H, bl.fc1, T.get(p + "mlp.fc1.weight", (int64_t)HID * C),
                   T.get(p + "mlp.fc1.bias", HID), C, HIDp, Cp, n_tile_for(HIDp),
-                  identity_rows(HIDp, HID));
-      if (!make_map_rows(&bl.fc1.mlp_map, bl.fc1.w, (uint64_t)HIDp, (uint64_t)Cp, 64))
+                  identity_rows(HIDp, HID), sp);
+      if (H->fused_mlp &&
+          !make_map_rows(&bl.fc1.mlp_map, bl.fc1.w, (uint64_t)HIDp, (uint64_t)Cp, 64))
         fail(S2S_ERR_CUDA, "cuTensorMapEncodeTiled failed for a weight operand");
       pack_linear(H, bl.fc2, T.get(p + "mlp.fc2.weight", (int64_t)C * HID),
-                  T.get(p + "mlp.fc2.bias", C), HID, Cp, HIDp, Cp, identity_rows(Cp, C));
+                  T.get(p + "mlp.fc2.bias", C), HID, Cp, HIDp, Cp, identity_rows(Cp, C), sp);
       bl.n1g = upload(H, padded(T.get(p + "norm1.weight", C), C, Cp));
       bl.n1b = upload(H, padded(T.get(p + "norm1.bias", C), C, Cp));
       bl.n2g = upload(H, padded(T.get(p + "norm2.weight", C), C, Cp));
@@ -424,15 +452,18 @@ void build_weights(s2s_handle* H, const TensorTable& T, std::vector<void*>& tmp)
     snprintf(pn, sizeof pn, "layers.%d.patch_embed.proj.weight", s);
     snprintf(pb, sizeof pb, "layers.%d.patch_embed.proj.bias", s);
     pack_conv(H, st.conv, T.get(cn, (int64_t)C * C * 9), T.get(cb, C), C, Cp, Cp, Cp,
-              identity_rows(Cp, C));
+              identity_rows(Cp, C), sp);
     pack_linear(H, st.pe, T.get(pn, (int64_t)C * C), T.get(pb, C), C, Cp, Cp, Cp,
-                identity_rows(Cp, C));
+                identity_rows(Cp, C), sp);
   }
   // head
   const int F = H->feat;
-  auto conv_plain = [&](TcWeight& tw, const std::string& name, int ci, int Cip, int co, int N) {
+  // body-plane convs (input: the two-term AO plane when split) and 64-channel head
+  // convs (single-term planes)
+  auto conv_plain = [&](TcWeight& tw, const std::string& name, int ci, int Cip, int co, int N,
+                        bool two = false) {
     pack_conv(H, tw, T.get(name + ".weight", (int64_t)co * ci * 9), T.get(name + ".bias", co), ci,
-              Cip, N, n_tile_for(N), identity_rows(N, co));
+              Cip, N, n_tile_for(N), identity_rows(N, co), two);
   };
   auto conv_shuffle = [&](TcWeight& tw, const std::string& name) {
     // GEMM column n = (2dy+dx)*F + f  <-  conv output channel 4f + 2dy + dx.
@@ -446,7 +477,7 @@ void build_weights(s2s_handle* H, const TensorTable& T, std::vector<void*>& tmp)
   switch (c.upsampler) {
     case S2S_PIXELSHUFFLE:
     case S2S_PIXELSHUFFLE_AUX:
-      conv_plain(H->cbu, "conv_before_upsample.0", C, Cp, F, F);
+      conv_plain(H->cbu, "conv_before_upsample.0", C, Cp, F, F, sp);
       for (int o = 0; o < octs; o++) conv_shuffle(H->oct[o], "upsample." + std::to_string(2 * o));
       conv_plain(H->last, "conv_last", F, F, 3, 32);
       if (c.upsampler == S2S_PIXELSHUFFLE_AUX) {
@@ -463,11 +494,11 @@ void build_weights(s2s_handle* H, const TensorTable& T, std::vector<void*>& tmp)
       break;
     case S2S_PIXELSHUFFLEDIRECT: {
       const int oc = 3 * c.scale * c.scale;
-      conv_plain(H->direct, "upsample.0", C, Cp, oc, pad_to(oc, 32));
+      conv_plain(H->direct, "upsample.0", C, Cp, oc, pad_to(oc, 32), sp);
       break;
     }
     case S2S_NEARESTCONV:
-      conv_plain(H->cbu, "conv_before_upsample.0", C, Cp, F, F);
+      conv_plain(H->cbu, "conv_before_upsample.0", C, Cp, F, F, sp);
       conv_plain(H->up1, "conv_up1", F, F, F, F);
       conv_plain(H->up2, "conv_up2", F, F, F, F);
       conv_plain(H->hr, "conv_hr", F, F, F, F);
@@ -513,8 +544,8 @@ int64_t plan_bytes(const s2s_handle* H, int B, int h, int w) {
   int64_t b = 0;
   b += (int64_t)B * 3 * hp * wp * 4;        // P
   b += 3 * T * Cp * 4;                      // F0, X, S
-  b += 3 * T * Cp * 2;                      // F0h, X16, AO
-  b += T * H->NQ * 2 + (H->fused_mlp ? 0 : T * H->HIDp * 2);  // QKV, H16 (unfused MLP)
+  b += 3 * T * H->Cs * 2;                   // F0h, X16, AO
+  b += T * H->NQs * 2 + (H->fused_mlp ? 0 : T * H->HIDs * 2);  // QKV, H16 (unfused MLP)
   b += 2 * T * 4;                           // window row tables
   b += T * 64 * 2 + 3 * T * s * s * 64 * 2; // head planes
   if (H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX)
@@ -593,18 +624,18 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
   const int hp = P->hp;
   const size_t T = (size_t)B * hp * wp;
   P->T = T;
-  const int Cp = H->Cp, s = H->cfg.scale;
+  const int Cp = H->Cp, Cs = H->Cs, s = H->cfg.scale;
   const size_t Th = (size_t)B * P->head_rows * wp;  // head plane tokens
   try {
     P->P = (float*)dalloc(*P, (size_t)B * 3 * hp * wp * 4);
     P->F0 = (float*)dalloc(*P, T * Cp * 4);
     P->X = (float*)dalloc(*P, T * Cp * 4);
     P->S = (float*)dalloc(*P, T * Cp * 4);
-    P->F0h = (__half*)dalloc(*P, T * Cp * 2);
-    P->X16 = (__half*)dalloc(*P, T * Cp * 2);
-    P->AO = (__half*)dalloc(*P, T * Cp * 2);
-    P->QKV = (__half*)dalloc(*P, T * H->NQ * 2);
-    if (!H->fused_mlp) P->H16 = (__half*)dalloc(*P, T * H->HIDp * 2);
+    P->F0h = (__half*)dalloc(*P, T * Cs * 2);
+    P->X16 = (__half*)dalloc(*P, T * Cs * 2);
+    P->AO = (__half*)dalloc(*P, T * Cs * 2);
+    P->QKV = (__half*)dalloc(*P, T * H->NQs * 2);
+    if (!H->fused_mlp) P->H16 = (__half*)dalloc(*P, T * H->HIDs * 2);
     for (int i = 0; i < 2; i++) P->rows[i] = (int*)dalloc(*P, (size_t)P->nwin[i] * 64 * 4);
     P->HA = (__half*)dalloc(*P, Th * 64 * 2);
     for (int i = 0; i < 3; i++) P->HB[i] = (__half*)dalloc(*P, Th * s * s * 64 * 2);
@@ -650,22 +681,22 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
   }
   // TMA maps over the activation buffers (the per-token GEMMs read the owned rows).
   bool ok = true;
-  ok &= make_map_rows(&P->mF0h, P->F0h + P->own_off * Cp, P->M_own, Cp, 128);
-  ok &= make_map_rows(&P->mX16, P->X16 + P->own_off * Cp, P->M_own, Cp, 128);
-  ok &= make_map_rows(&P->mX16s, P->X16 + P->sh_off * Cp, P->M_sh, Cp, 128);
+  ok &= make_map_rows(&P->mF0h, P->F0h + P->own_off * Cs, P->M_own, Cs, 128);
+  ok &= make_map_rows(&P->mX16, P->X16 + P->own_off * Cs, P->M_own, Cs, 128);
+  ok &= make_map_rows(&P->mX16s, P->X16 + P->sh_off * Cs, P->M_sh, Cs, 128);
   if (band) {
-    ok &= make_map_rows(&P->mX16t, P->X16 + P->sh_off * Cp, (uint64_t)4 * wp, Cp, 128);
-    ok &= make_map_rows(&P->mX16b, P->X16 + (P->own_off + P->M_own) * Cp, (uint64_t)4 * wp, Cp,
+    ok &= make_map_rows(&P->mX16t, P->X16 + P->sh_off * Cs, (uint64_t)4 * wp, Cs, 128);
+    ok &= make_map_rows(&P->mX16b, P->X16 + (P->own_off + P->M_own) * Cs, (uint64_t)4 * wp, Cs,
                         128);
   }
-  ok &= make_map_rows(&P->mAO, P->AO + P->own_off * Cp, P->M_own, Cp, 128);
-  if (P->H16) ok &= make_map_rows(&P->mH16, P->H16 + P->own_off * H->HIDp, P->M_own, H->HIDp, 128);
+  ok &= make_map_rows(&P->mAO, P->AO + P->own_off * Cs, P->M_own, Cs, 128);
+  if (P->H16) ok &= make_map_rows(&P->mH16, P->H16 + P->own_off * H->HIDs, P->M_own, H->HIDs, 128);
   {
     int bw, bh;
     conv_box(wp, &bw, &bh);
-    ok &= make_map_nhwc(&P->cX16, P->X16 + (size_t)P->conv_row0 * wp * Cp, B, P->conv_H, wp, Cp,
+    ok &= make_map_nhwc(&P->cX16, P->X16 + (size_t)P->conv_row0 * wp * Cs, B, P->conv_H, wp, Cs,
                         bw, bh);
-    ok &= make_map_nhwc(&P->cAO, P->AO + (size_t)P->head_row0 * wp * Cp, B, P->head_rows, wp, Cp,
+    ok &= make_map_nhwc(&P->cAO, P->AO + (size_t)P->head_row0 * wp * Cs, B, P->head_rows, wp, Cs,
                         bw, bh);
     ok &= make_map_nhwc(&P->cHA, P->HA, B, P->head_rows, wp, 64, bw, bh);
   }
@@ -782,6 +813,20 @@ GemmArgs conv_args(int B, int H, int W, int Cip, int N, const Epi& e, int y0, in
   return a;
 }
 
+// Two-term operands: A rows [hi | lo] of `kc` 64-column chunks each, B [hi | hi | lo]
+// (three K blocks per tap for a convolution).
+void two_term(GemmArgs& a, bool split) {
+  if (!split) return;
+  if (a.conv) {
+    a.amod = 2 * a.kc;
+    a.kc *= 3;
+    a.K *= 3;
+  } else {
+    a.amod = 2 * (a.K / 64);
+    a.K *= 3;
+  }
+}
+
 // The STORE_ROWS outputs and the post-norm residual of a launch, as TMA maps.
 OutMaps out_maps(Plan* P, const GemmArgs& a) {
   OutMaps om;
@@ -894,17 +939,20 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
   H->fwd_launches = 0;
   Launcher L{H, st};
   const int C = c.embed, Cp = H->Cp, hp = P->hp, wp = P->wp, s = c.scale, F = H->feat;
+  // fp16 operand rows: stride Cs, and with two-term operands the lo terms Cp after hi
+  const int Cs = H->Cs, lo = H->split ? Cp : 0;
+  const bool sp = H->split;
   const int M = P->M_own;
   const bool band = P->band != 0;
   float* const X = P->X + P->own_off * Cp;       // owned rows of the residual stream
-  __half* const X16 = P->X16 + P->own_off * Cp;
+  __half* const X16 = P->X16 + P->own_off * Cs;
   float* const S = P->S + P->own_off * Cp;
   // Halo transfers run on the side stream behind an event, so they start only once
   // every kernel before them has completed (kernels signal their dependents early).
   auto exchange = [&](const char* name, __half* buf, int n, bool cyclic, bool zero_edges) {
     ck(cudaEventRecord(H->fork, st), "fork");
     ck(cudaStreamWaitEvent(H->side, H->fork, 0), "fork");
-    L.comm(name, H->side, [&] { halo_exchange(H, P, buf, Cp, n, cyclic, zero_edges, H->side); });
+    L.comm(name, H->side, [&] { halo_exchange(H, P, buf, Cs, n, cyclic, zero_edges, H->side); });
     ck(cudaEventRecord(H->join, H->side), "join");
     ck(cudaStreamWaitEvent(st, H->join, 0), "join");
   };
@@ -918,7 +966,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
   }
   L.run("conv_first", [&] {
     return launch_conv3_small(P->P, H->cf_w, H->cf_b, B, hp, wp, C, 0, 0.0f, P->F0, Cp, P->F0h,
-                              Cp, st);
+                              Cs, lo, st);
   });
   // 2. top patch_embed: 1x1 + LayerNorm -> X, X16 and the stage input S.
   {
@@ -931,10 +979,12 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.o32 = X;
     e.ld32 = Cp;
     e.o16 = X16;
-    e.ld16 = Cp;
+    e.ld16 = Cs;
+    e.lo_off = lo;
     e.o32b = S;
     e.ld32b = Cp;
     GemmArgs a = gemm_args(M, Cp, Cp, e);
+    two_term(a, sp);
     L.run("gemm_patch_embed", [&] { return launch_gemm(P->mF0h, H->pe.map, out_maps(P, a), a, Cp, st); });
   }
   for (int si = 0; si < c.n_depths; si++) {
@@ -950,9 +1000,11 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.act = ACT_QKNORM;  // normalised q (times the logit scale) and k for the attention
         e.qk_scale = bl.ls;
         e.qk_dp = H->DP;
-        e.o16 = P->QKV + off * H->NQ;
-        e.ld16 = H->NQ;
+        e.o16 = P->QKV + off * H->NQs;
+        e.ld16 = H->NQs;
+        e.lo_off = sp ? H->NQ : 0;
         GemmArgs a = gemm_args(rows, H->NQ, Cp, e);
+        two_term(a, sp);
         L.run("gemm_qkv", [&] { return launch_gemm(mA, bl.qkv.map, out_maps(P, a), a, bl.qkv.BN, st); });
       };
       if (band && sh) {
@@ -962,7 +1014,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         ck(cudaEventRecord(H->fork, st), "fork");
         ck(cudaStreamWaitEvent(H->side, H->fork, 0), "fork");
         L.comm("halo_shift", H->side,
-               [&] { halo_exchange(H, P, P->X16, Cp, 4, true, false, H->side); });
+               [&] { halo_exchange(H, P, P->X16, Cs, 4, true, false, H->side); });
         ck(cudaEventRecord(H->join, H->side), "join");
         qkv(P->mX16, P->own_off, M);
         ck(cudaStreamWaitEvent(st, H->join, 0), "join");
@@ -973,8 +1025,8 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       }
       L.run("window_attention", [&] {
         return launch_window_attention(P->QKV, P->AO, bl.cpb, P->rows[k], P->nwin[k],
-                                       H->heads, H->hd, H->DP, Cp, P->nwh_l[k], wp / 8, P->ghp,
-                                       wp, sh, P->wh_off[k], st);
+                                       H->heads, H->hd, H->DP, Cs, H->NQs, sp, H->NQ, lo,
+                                       P->nwh_l[k], wp / 8, P->ghp, wp, sh, P->wh_off[k], st);
       });
       {  // proj + norm1 + residual, in place
         Epi e = epi0();
@@ -988,8 +1040,10 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.o32 = X;
         e.ld32 = Cp;
         e.o16 = X16;
-        e.ld16 = Cp;
+        e.ld16 = Cs;
+        e.lo_off = lo;
         GemmArgs a = gemm_args(M, Cp, Cp, e);
+        two_term(a, sp);
         L.run("gemm_proj", [&] { return launch_gemm(P->mAO, bl.proj.map, out_maps(P, a), a, Cp, st); });
       }
       if (H->fused_mlp) {  // fc1 + GELU + fc2 + norm2 + residual in one kernel
@@ -1008,7 +1062,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
           eo.o32 = X;
           eo.ld32 = Cp;
           eo.o16 = X16;
-          eo.ld16 = Cp;
+          eo.ld16 = Cs;
           const OutMaps om = out_maps(P, gemm_args(M, Cp, Cp, eo));
           return launch_mlp(P->mX16, bl.fc1.mlp_map, bl.fc2.map, om.o32, om.o16, m, Cp, H->HIDp,
                             st);
@@ -1018,9 +1072,11 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
           Epi e = epi0();
           e.bias = bl.fc1.b;
           e.act = ACT_GELU;
-          e.o16 = P->H16 + P->own_off * H->HIDp;
-          e.ld16 = H->HIDp;
+          e.o16 = P->H16 + P->own_off * H->HIDs;
+          e.ld16 = H->HIDs;
+          e.lo_off = sp ? H->HIDp : 0;
           GemmArgs a = gemm_args(M, H->HIDp, Cp, e);
+          two_term(a, sp);
           L.run("gemm_fc1", [&] { return launch_gemm(P->mX16, bl.fc1.map, out_maps(P, a), a, bl.fc1.BN, st); });
         }
         {  // fc2 + norm2 + residual, in place
@@ -1035,8 +1091,10 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
           e.o32 = X;
           e.ld32 = Cp;
           e.o16 = X16;
-          e.ld16 = Cp;
+          e.ld16 = Cs;
+          e.lo_off = lo;
           GemmArgs a = gemm_args(M, Cp, H->HIDp, e);
+          two_term(a, sp);
           L.run("gemm_fc2", [&] { return launch_gemm(P->mH16, bl.fc2.map, out_maps(P, a), a, Cp, st); });
         }
       }
@@ -1047,9 +1105,11 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       Epi e = epi0();
       e.bias = stg.conv.b;
       e.n_valid = C;
-      e.o16 = P->AO + (size_t)P->conv_row0 * wp * Cp;
-      e.ld16 = Cp;
+      e.o16 = P->AO + (size_t)P->conv_row0 * wp * Cs;
+      e.ld16 = Cs;
+      e.lo_off = lo;
       GemmArgs a = conv_args(B, P->conv_H, wp, Cp, Cp, e, P->conv_y0, P->conv_y1);
+      two_term(a, sp);
       L.run("conv_stage", [&] { return launch_gemm(P->cX16, stg.conv.map, out_maps(P, a), a, Cp, st); });
     }
     {
@@ -1070,7 +1130,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.o32 = X;
         e.ld32 = Cp;
         e.o16 = X16;
-        e.ld16 = Cp;
+        e.ld16 = Cs;
         e.o32b = S;
         e.ld32b = Cp;
       } else {  // + final norm, image order, fp16 operand of conv_after_body
@@ -1078,9 +1138,11 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         e.ln_b = H->nrm_b;
         e.ln_n = C;
         e.o16 = X16;
-        e.ld16 = Cp;
+        e.ld16 = Cs;
       }
+      e.lo_off = lo;
       GemmArgs a = gemm_args(M, Cp, Cp, e);
+      two_term(a, sp);
       L.run(last ? "gemm_stage_pe_norm" : "gemm_stage_pe",
             [&] { return launch_gemm(P->mAO, stg.pe.map, out_maps(P, a), a, Cp, st); });
     }
@@ -1093,17 +1155,21 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.n_valid = C;
     e.res_post = P->F0 + (size_t)P->conv_row0 * wp * Cp;
     e.ld_res_post = Cp;
-    e.o16 = P->AO + (size_t)P->conv_row0 * wp * Cp;
-    e.ld16 = Cp;
+    e.o16 = P->AO + (size_t)P->conv_row0 * wp * Cs;
+    e.ld16 = Cs;
+    e.lo_off = lo;
     GemmArgs a = conv_args(B, P->conv_H, wp, Cp, Cp, e, P->conv_y0, P->conv_y1);
+    two_term(a, sp);
     L.run("conv_after_body", [&] { return launch_gemm(P->cX16, H->cab.map, out_maps(P, a), a, Cp, st); });
   }
   // 4. head, on its own plane: head_rows x wp (the whole padded plane unless banded).
   if (band) exchange("halo_head", P->AO, 4, false, false);
   const int hh0 = P->head_rows;
+  // `two`: the input plane is the body's two-term AO plane
   auto conv_to = [&](const char* name, const CUtensorMap& mapA, const TcWeight& tw, int Hh, int Ww,
-                     int Cip, Epi e) {
+                     int Cip, Epi e, bool two = false) {
     GemmArgs a = conv_args(B, Hh, Ww, Cip, tw.N, e, 0, Hh);
+    two_term(a, two && sp);
     L.run(name, [&] { return launch_gemm(mapA, tw.map, out_maps(P, a), a, tw.BN, st); });
   };
   // a 64-channel conv over head plane HB[i] at resolution 2^r, from kx patches when
@@ -1125,7 +1191,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
     e.slope = 0.01f;
     e.o16 = P->HA;
     e.ld16 = F;
-    conv_to("conv_before_upsample", P->cAO, H->cbu, hh0, wp, Cp, e);
+    conv_to("conv_before_upsample", P->cAO, H->cbu, hh0, wp, Cp, e, true);
   };
   // conv_last over head plane HB[i] at resolution 2^r: from kx patches of the plane
   // when its conv box allows them (three input fetches per tile instead of nine)
@@ -1163,7 +1229,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         });
         L.run("conv_bicubic", [&] {
           return launch_conv3_small(P->BIC, H->cbic_w, H->cbic_b, B, hp * s, wp * s, F, 0, 0.0f,
-                                    P->BICF, F, nullptr, 0, st);
+                                    P->BICF, F, nullptr, 0, 0, st);
         });
         Epi e = epi0();
         e.bias = H->aux.b;
@@ -1176,7 +1242,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         conv_to("conv_aux", P->cHA, H->aux, hp, wp, F, e);
         L.run("conv_after_aux", [&] {
           return launch_conv3_small(P->AUXRAW, H->caa_w, H->caa_b, B, hp, wp, F, 2, 0.01f,
-                                    nullptr, 0, P->HB[2], F, st);
+                                    nullptr, 0, P->HB[2], F, 0, st);
         });
         src = &P->cHB[2][0];
       }
@@ -1205,7 +1271,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       e.crop_h = P->crop_rows * s;
       e.crop_w = w * s;
       set_final(H, e);
-      conv_to("conv_upsample_direct", P->cAO, H->direct, hh0, wp, Cp, e);
+      conv_to("conv_upsample_direct", P->cAO, H->direct, hh0, wp, Cp, e, true);
       break;
     }
     case S2S_NEARESTCONV: {
@@ -1445,7 +1511,21 @@ int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, 
     g_create_error = "s2s_create: unsupported padded widths";
     return S2S_ERR_UNSUPPORTED;
   }
-  const bool can_fuse = (H->Cp == 192 && H->HIDp == 384) || (H->Cp == 64 && H->HIDp == 128);
+  // Two-term operands by default for the narrow (Cp = 64) networks; S2S_SPLIT=0 / 1
+  // (validation switch) turns them off / on for every width.
+  H->split = H->Cp == 64;
+  {
+    const char* v = getenv("S2S_SPLIT");
+    if (v && strcmp(v, "0") == 0) H->split = false;
+    if (v && strcmp(v, "1") == 0) H->split = true;
+    if (g_create_flags.split >= 0) H->split = g_create_flags.split != 0;
+  }
+  H->Cs = H->split ? 2 * H->Cp : H->Cp;
+  H->NQs = H->split ? 2 * H->NQ : H->NQ;
+  H->HIDs = H->split ? 2 * H->HIDp : H->HIDp;
+  // the fused MLP keeps its hidden activation in single-term fp16
+  const bool can_fuse = !H->split && ((H->Cp == 192 && H->HIDp == 384) ||
+                                      (H->Cp == 64 && H->HIDp == 128));
   H->fused_mlp = can_fuse;
   {
     const char* f = getenv("S2S_UNFUSED_MLP");  // validation switch: the two-GEMM MLP path
@@ -1577,7 +1657,7 @@ int s2s_profile_report(s2s_handle* H, char* buf, int cap, int reset) {
   return (int)s.size() + 1;
 }
 
-int64_t s2s_launch_count(const s2s_handle* H) { return H ? H->launches : 0; }
+int64_t s2s_launch_count(const s2s_handle* H) { return H ? H->launches.load() : 0; }
 
 int s2s_debug_stop_after(s2s_handle* H, int64_t launches) {
   if (!H) return S2S_ERR_INVALID;
@@ -1597,11 +1677,11 @@ int64_t s2s_debug_read(s2s_handle* H, const char* name, float* host, int64_t cap
   else if (k == "F0") { p = P.F0; n = T * Cp; }
   else if (k == "X") { p = P.X; n = T * Cp; }
   else if (k == "S") { p = P.S; n = T * Cp; }
-  else if (k == "F0h") { p = P.F0h; n = T * Cp; half = true; }
-  else if (k == "X16") { p = P.X16; n = T * Cp; half = true; }
-  else if (k == "QKV") { p = P.QKV; n = T * H->NQ; half = true; }
-  else if (k == "AO") { p = P.AO; n = T * Cp; half = true; }
-  else if (k == "H16") { p = P.H16; n = T * H->HIDp; half = true; }
+  else if (k == "F0h") { p = P.F0h; n = T * H->Cs; half = true; }
+  else if (k == "X16") { p = P.X16; n = T * H->Cs; half = true; }
+  else if (k == "QKV") { p = P.QKV; n = T * H->NQs; half = true; }
+  else if (k == "AO") { p = P.AO; n = T * H->Cs; half = true; }
+  else if (k == "H16") { p = P.H16; n = T * H->HIDs; half = true; }
   else if (k == "HA") { p = P.HA; n = T * 64; half = true; }
   else if (k == "HB0") { p = P.HB[0]; n = T * s * s * 64; half = true; }
   else if (k == "HB1") { p = P.HB[1]; n = T * s * s * 64; half = true; }
@@ -1771,7 +1851,7 @@ int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors
   std::string rep;
   bool all_ok = true;
   int status = S2S_OK;
-  s2s_handle* hs[3] = {nullptr, nullptr, nullptr};
+  s2s_handle* hs[4] = {nullptr, nullptr, nullptr, nullptr};
   auto check = [&](const char* name, double err, double tol) {
     char b[192];
     const bool ok = err <= tol;
@@ -1782,9 +1862,10 @@ int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors
   };
   // handle k with the given validation switches; false (and the error in the report)
   // when it cannot be made
-  auto make = [&](int k, int unfused_mlp, int no_patch) -> bool {
+  auto make = [&](int k, int unfused_mlp, int no_patch, int split = -1) -> bool {
     g_create_flags.unfused_mlp = unfused_mlp;
     g_create_flags.no_patch = no_patch;
+    g_create_flags.split = split;
     const int rc = s2s_create(cfg, tensors, n_tensors, device, &hs[k]);
     g_create_flags = CreateFlags{};
     if (rc != S2S_OK) {
@@ -1840,6 +1921,10 @@ int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors
   go = go && make(2, 1, 0) &&
        ran(hs[2], s2s_forward(hs[2], h, w, in.data(), other.data(), nullptr), "forward");
   if (go) check("fused_vs_unfused_mlp", maxabs(other.data(), eager.data(), nout), 2e-3);
+  // two-term operands against single-term ones (the other of the two for this width)
+  go = go && make(3, 1, 0, hs[0]->split ? 0 : 1) &&
+       ran(hs[3], s2s_forward(hs[3], h, w, in.data(), other.data(), nullptr), "forward");
+  if (go) check("two_term_vs_single_term", maxabs(other.data(), eager.data(), nout), 2e-2);
   for (s2s_handle*& x : hs)
     if (x) s2s_destroy(x);
   if (report && cap > 0) {

@@ -170,11 +170,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             mbar_arrive_expect_tx(&full[s], bres ? A_BYTES : A_BYTES + B_BYTES);
             if (!a.conv) {
-              tma_load_2d(sA + s * A_SLOT, &mapA, &full[s], k * 64, m0);
+              const int ak = a.amod ? k % a.amod : k;
+              tma_load_2d(sA + s * A_SLOT, &mapA, &full[s], ak * 64, m0);
             } else {
               const int tap = k / a.kc, cc = k - tap * a.kc;
               const int ky = tap / 3, kx = tap - ky * 3;
-              tma_load_4d(sA + s * A_SLOT, &mapA, &full[s], cc * 64, x0 + kx - 1, y0 + ky - 1,
+              const int ac = a.amod ? cc % a.amod : cc;
+              tma_load_4d(sA + s * A_SLOT, &mapA, &full[s], ac * 64, x0 + kx - 1, y0 + ky - 1,
                           bimg);
             }
             if (!bres) tma_load_2d(sB + s * B_SLOT, &mapB, &full[s], k * 64, n0);
@@ -368,6 +370,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) bulk_wait_read<1>();  // this buffer's store two chunks ago
           __syncwarp();
         }
+        // two-term output: hi and lo take both fp16 tiles, free once every store read them
+        if (e.lo_off) {
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+        }
         const int cl0 = c * 32;
 #pragma unroll
         for (int u = 0; u < 8; u++) {
@@ -437,6 +444,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        uint8_t* const f16h = e.lo_off ? wbuf + F16OFF : f16;  // hi tile
+        uint8_t* const f16l = wbuf + F16OFF + 2048;              // lo tile (two-term only)
         if (e.o16) {
 #pragma unroll
           for (int u = 0; u < 4; u++) {
@@ -444,9 +453,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             __half2 h1 = __floats2half2_rn(v[8 * u + 2], v[8 * u + 3]);
             __half2 h2 = __floats2half2_rn(v[8 * u + 4], v[8 * u + 5]);
             __half2 h3 = __floats2half2_rn(v[8 * u + 6], v[8 * u + 7]);
-            *reinterpret_cast<uint4*>(f16 + lane * 64 + ((u ^ sw64) << 4)) =
+            *reinterpret_cast<uint4*>(f16h + lane * 64 + ((u ^ sw64) << 4)) =
                 make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
                            *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+            if (e.lo_off) {
+              // the remainder each fp16 value left out, itself in fp16
+              const __half2 hs[4] = {h0, h1, h2, h3};
+              uint32_t lw[4];
+#pragma unroll
+              for (int m = 0; m < 4; m++) {
+                const float2 hf = __half22float2(hs[m]);
+                const __half2 l = __floats2half2_rn(v[8 * u + 2 * m] - hf.x,
+                                                    v[8 * u + 2 * m + 1] - hf.y);
+                lw[m] = *reinterpret_cast<const uint32_t*>(&l);
+              }
+              *reinterpret_cast<uint4*>(f16l + lane * 64 + ((u ^ sw64) << 4)) =
+                  make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            }
           }
         }
         fence_proxy_async_smem();
@@ -454,7 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           if (e.o32) box_store(&om.o32, f32, n0 + cl0);
           if (e.o32b) box_store(&om.o32b, f32, n0 + cl0);
-          if (e.o16) box_store(&om.o16, f16, n0 + cl0);
+          if (e.o16) box_store(&om.o16, f16h, n0 + cl0);
+          if (e.o16 && e.lo_off) box_store(&om.o16, f16l, e.lo_off + n0 + cl0);
           bulk_commit();
         }
       }
@@ -608,19 +632,11 @@ cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const Out
   const size_t smem = 1024 + (size_t)NA * A_SLOT + (size_t)STAGES * B_SLOT + kEpiWarps * WB +
                       3 * BN * 4 + kEpiWarps * 32 * 4 * 4 + (2 * NA + 6 + 2 * kEpiWarps) * 8 +
                       16;
-  static int ctas = 0;  // resident CTAs per device (SMs x CTAs per SM), one process per GPU
-  if (ctas == 0) {
-    cudaError_t err = cudaFuncSetAttribute(k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (err != cudaSuccess) return err;
-    int dev = 0, sms = 0, occ = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH>, kThreads, smem);
-    if (err != cudaSuccess) return err;
-    if (occ < 1) return cudaErrorInvalidConfiguration;
-    ctas = sms * occ;
-  }
+  static LaunchSetup setup;  // resident CTAs (SMs x CTAs per SM), per device
+  int ctas = 0;
+  const cudaError_t err = resident_ctas(
+      setup, k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH>, kThreads, smem, &ctas);
+  if (err != cudaSuccess) return err;
   const int NT = a.N / BN;
   const int tiles_m = a.conv ? a.B * a.tiles_x * a.tiles_y : (a.M + 127) / 128;
   const long tiles = (long)tiles_m * NT;
@@ -673,9 +689,12 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   S2S_VARIANT(192, 3, ACT_NONE, false, 1, STORE_ROWS)
   S2S_VARIANT(192, 3, ACT_NONE, true, 1, STORE_ROWS)
   S2S_VARIANT(192, 3, ACT_NONE, false, 2, STORE_ROWS)
-  // QKV (fp16 output only, B resident): A gets a six-slot ring of its own
-  if (BN == 192 && act == ACT_QKNORM && !ln && res == 0 && store == STORE_ROWS)
+  // QKV (fp16 output only, B resident): A gets a six-slot ring of its own; with
+  // two-term operands (K = 3 x 192) B streams through the ring
+  if (BN == 192 && act == ACT_QKNORM && !ln && res == 0 && store == STORE_ROWS && a.K / 64 <= 3)
     return launch_t<192, 3, ACT_QKNORM, false, 0, STORE_ROWS, 6, kWarpBufF16>(mapA, mapB, om, a, st);
+  if (BN == 192 && act == ACT_QKNORM && !ln && res == 0 && store == STORE_ROWS)
+    return launch_t<192, 3, ACT_QKNORM, false, 0, STORE_ROWS, 0, kWarpBufF16>(mapA, mapB, om, a, st);
   S2S_VARIANT(96, 4, ACT_QKNORM, false, 0, STORE_ROWS)
   // embed 60 (Cp 64) and the 64-channel head convs
   S2S_VARIANT(64, 4, ACT_NONE, false, 0, STORE_ROWS)

@@ -43,6 +43,10 @@ struct Epi {
   int ld_res_post;
   // Columns [n_valid, N) hold zeros (padded weights, bias and norms make them so).
   int n_valid;
+  // Two-term fp16 output (STORE_ROWS): besides hi = fp16(v) at column n, the
+  // remainder lo = fp16(v - hi) goes to column lo_off + n of the same o16 rows, so a
+  // later GEMM can read both terms as one operand row [hi | lo]. 0: hi only.
+  int lo_off;
   // Outputs. STORE_ROWS writes them through OutMaps (o32, o32b, o16); the pointers
   // say which are present. STORE_SHUFFLE2 writes o16 directly.
   float* o32;
@@ -72,6 +76,11 @@ struct GemmArgs {
   // conv with kc == 1 and boxw <= 32: mapA's boxes are (boxh + 2)-row patches, one per
   // kx, each serving its three ky taps (launch_gemm supports it for the plane store)
   int patch;
+  // Two-term operands: A's K-slice for slice k (GEMM), or for chunk cc of a tap
+  // (conv), is k % amod (cc % amod). With A rows [hi | lo] (amod = 2 * kc) and B
+  // packed [W_hi | W_hi | W_lo] (K = 3 * kc slices), the one accumulation is
+  // hi*W_hi + lo*W_hi + hi*W_lo. 0: no wrap.
+  int amod;
   Epi epi;
 };
 

@@ -60,7 +60,7 @@ constexpr int kConvGroups = 8;  // channel groups per block (blockDim = 32 x 8)
 __global__ void __launch_bounds__(256) k_conv3_small(
     const float* __restrict__ in, const float* __restrict__ wgt, const float* __restrict__ bias,
     int B, int H, int W, int co_n, int act, float slope, float* __restrict__ o32, int ld32,
-    __half* __restrict__ o16, int ld16) {
+    __half* __restrict__ o16, int ld16, int lo16) {
   // weights of output channels (2p, 2p + 1) side by side: one float2 per tap feeds a
   // packed two-channel fma
   __shared__ float2 sw2[kConvGroups * 4][27];
@@ -142,13 +142,28 @@ __global__ void __launch_bounds__(256) k_conv3_small(
         u.z = *reinterpret_cast<uint32_t*>(&h2);
         u.w = *reinterpret_cast<uint32_t*>(&h3);
         *reinterpret_cast<uint4*>(o16 + p * ld16 + c0) = u;
+        if (lo16) {  // two-term operand: the remainder of each fp16 value, at lo16
+          const __half2 hs[4] = {h0, h1, h2, h3};
+          uint32_t lw[4];
+#pragma unroll
+          for (int m = 0; m < 4; m++) {
+            const float2 f = __half22float2(hs[m]);
+            const __half2 l = __floats2half2_rn(acc[2 * m] - f.x, acc[2 * m + 1] - f.y);
+            lw[m] = *reinterpret_cast<const uint32_t*>(&l);
+          }
+          *reinterpret_cast<uint4*>(o16 + p * ld16 + lo16 + c0) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
       }
     } else {
 #pragma unroll
       for (int j = 0; j < 8; j++)
         if (j < nv) {
           if (o32) o32[p * ld32 + c0 + j] = acc[j];
-          if (o16) o16[p * ld16 + c0 + j] = __float2half_rn(acc[j]);
+          if (o16) {
+            const __half hv = __float2half_rn(acc[j]);
+            o16[p * ld16 + c0 + j] = hv;
+            if (lo16) o16[p * ld16 + lo16 + c0 + j] = __float2half_rn(acc[j] - __half2float(hv));
+          }
         }
     }
   }
@@ -277,16 +292,17 @@ cudaError_t launch_pad_band(const float* x, float* y, int c, int h, int w, int h
 
 cudaError_t launch_conv3_small(const float* in, const float* wgt, const float* bias, int B, int H,
                                int W, int co_n, int act, float slope, float* o32, int ld32,
-                               __half* o16, int ld16, cudaStream_t st) {
+                               __half* o16, int ld16, int lo16, cudaStream_t st) {
   // vector stores: 8-channel groups start 32-byte (fp32) / 16-byte (fp16) aligned
-  if ((o32 && (ld32 % 4 || (uintptr_t)o32 % 16)) || (o16 && (ld16 % 8 || (uintptr_t)o16 % 16)))
+  if ((o32 && (ld32 % 4 || (uintptr_t)o32 % 16)) ||
+      (o16 && (ld16 % 8 || lo16 % 8 || (uintptr_t)o16 % 16)))
     return cudaErrorInvalidValue;
   const int gy = (co_n + kConvGroups * 8 - 1) / (kConvGroups * 8);
   const size_t tiles = (size_t)B * H * ((W + 31) / 32);
   // a few blocks per SM, each walking many pixel tiles: the weight staging is paid once
   const unsigned gx = (unsigned)std::min<size_t>(tiles, (size_t)148 * 3);
   return launch_pdl(k_conv3_small, dim3(gx, gy), dim3(32, kConvGroups), 0, st, in, wgt, bias, B, H,
-                    W, co_n, act, slope, o32, ld32, o16, ld16);
+                    W, co_n, act, slope, o32, ld32, o16, ld16, lo16);
 }
 
 cudaError_t launch_zero_cols_f16(__half* x, size_t rows, int c0, int ld, cudaStream_t st) {

@@ -418,21 +418,11 @@ cudaError_t launch_mlp_t(const CUtensorMap& mX, const CUtensorMap& mW1, const CU
                          const CUtensorMap& mX32, const CUtensorMap& mX16o, const MlpArgs& a,
                          cudaStream_t st) {
   using Cfg = MlpCfg<CP, HP, STAGES>;
-  static int ctas = 0;
-  if (ctas == 0) {
-    cudaError_t err = cudaFuncSetAttribute(k_mlp<CP, HP, STAGES>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)Cfg::SMEM);
-    if (err != cudaSuccess) return err;
-    int dev = 0, sms = 0, occ = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_mlp<CP, HP, STAGES>, kMlpThreads,
-                                                        Cfg::SMEM);
-    if (err != cudaSuccess) return err;
-    if (occ < 1) return cudaErrorInvalidConfiguration;
-    ctas = sms * occ;
-  }
+  static LaunchSetup setup;
+  int ctas = 0;
+  const cudaError_t err =
+      resident_ctas(setup, k_mlp<CP, HP, STAGES>, kMlpThreads, Cfg::SMEM, &ctas);
+  if (err != cudaSuccess) return err;
   const int tiles = (a.M + 127) / 128;
   const int G = tiles < ctas ? tiles : ctas;
   return launch_pdl(k_mlp<CP, HP, STAGES>, dim3(G), dim3(kMlpThreads), Cfg::SMEM, st, mX, mW1, mW2,

@@ -87,9 +87,9 @@ extern "C" int s2s_window_attention_noalloc(s2s_handle* H, int stage, int block,
     ck(cudaGetLastError(), "window_rows");
     const Block& bl = H->stages[stage].blocks[block];
     ck(launch_window_attention((const __half*)d_qkv, (__half*)d_out, bl.cpb, rows,
-                               batch * (hp / 8) * (wp / 8), H->heads, H->hd, H->DP, ld_out, hp / 8,
-                               wp / 8, hp, wp, shift, 0, st),
+                               batch * (hp / 8) * (wp / 8), H->heads, H->hd, H->DP, ld_out, H->NQ,
+                               0, 0, 0, hp / 8, wp / 8, hp, wp, shift, 0, st),
        "window_attention");
-    H->launches += 2;
+    H->launches.fetch_add(2, std::memory_order_relaxed);
   });
 }

@@ -1,9 +1,11 @@
 """The CUDA path against the oracle and the published network, through the C ABI.
 
 Tolerance (north_star, and the reference's tests/parity.rs:33): max-abs <= 2e-3 on
-the [0,1]-clamped output, and <= 1 8-bit level on >= 99.9% of values. The kernels
-compute in fp16 operands with fp32 accumulation; the residual stream, LayerNorm,
-softmax and every epilogue stay fp32.
+the [0,1]-clamped output, and <= 1 8-bit level on >= 99.9% of values, for every
+network and case. The kernels compute in fp16 operands with fp32 accumulation; the
+residual stream, LayerNorm, softmax and every epilogue stay fp32. The 60-wide
+network carries two-term operands (hi + lo fp16, about 21 bits): with single fp16
+operands it moved by up to 5e-3 on the perturbed-weight cases.
 """
 import importlib
 
@@ -27,13 +29,6 @@ def backend_for(task, wseed=0, perturb=False):
     return _handles[key]
 
 
-# The 60-wide lightweight network is the precision-sensitive one: with fp16 operands
-# its BASELINE configuration (seed-0 weights, 64x64) lands at ~1.4e-3, inside the
-# 2e-3 gate, but the extra stress cases with perturbed biases and norms reach ~5e-3.
-# Those are gated on the 8-bit criterion and this documented looser bound.
-TOL_LW_STRESS = 6e-3
-
-
 def check(got, want, what, frac=1e-3, tol=TOL):
     raw, clamped, off = parity_report(got, want)
     print(f"{what}: max-abs raw {raw:.3e} clamped {clamped:.3e} >1-level {off:.2e}")
@@ -49,8 +44,7 @@ def test_golden_fixture(case):
     h, w, s, win, x, y, aux = load_fixture(case["name"])
     out = gpu.forward(h, w, adjust(wt, x))
     assert out.shape == y.shape and np.isfinite(out).all()
-    stress = case["task"] == "lightweight_sr" and case["perturb"]
-    check(out, y, case["name"], tol=TOL_LW_STRESS if stress else TOL)
+    check(out, y, case["name"])
     if aux is not None:
         got = gpu.aux()
         assert got is not None and got.shape == aux.shape
@@ -85,7 +79,7 @@ def test_forward_matches_oracle(task, h, w):
     a = adjust(wt, x)
     out = gpu.forward(h, w, a)
     ref, raux = O.forward(wt, h, w, a)
-    check(out, ref, f"{task} {h}x{w}", tol=TOL_LW_STRESS if task == "lightweight_sr" else TOL)
+    check(out, ref, f"{task} {h}x{w}")
     if raux is not None:
         check(gpu.aux(), raux, f"{task} {h}x{w} aux")
 
@@ -182,6 +176,70 @@ def test_classical_x4_full_size_matches_oracle():
     out = gpu.forward(240, 320, x)
     ref, _ = oracle().forward(wt, 240, 320, x)
     check(out, ref, "classical-x4 240x320")
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", ["classical-x2", "realworld-x4"])
+def test_baseline_single_image_full_size_matches_oracle(name):
+    """BASELINE's other whole-image configurations at their full size: classical-x2
+    256x256 -> 512x512 and realworld-x4 512x512 -> 2048x2048 (its head convs run on
+    2080x2080 planes), seed-0 weights, the committed input recipes."""
+    wl = importlib.import_module("swin2sr_b200.workloads")
+    spec = wl.WORKLOADS[name]
+    wt, gpu = backend_for(spec["task"], 0, False)
+    h, w = spec["h"], spec["w"]
+    x = wl.adjust(wl.make_input(name), wt)[0]
+    out = gpu.forward(h, w, x)
+    ref, _ = oracle().forward(wt, h, w, x)
+    check(out, ref, f"{name} {h}x{w}")
+
+
+@pytest.mark.slow
+def test_compressed_x4_full_batch_matches_oracle():
+    """BASELINE's compressed-x4 batch: 256 48x48 images in one batched forward (802 816
+    tokens in one plane). Sixteen members spread over the batch are checked against the
+    oracle, output and aux; every member equals its own single-image forward (the batch
+    is independent images), checked on the same sixteen."""
+    wl = importlib.import_module("swin2sr_b200.workloads")
+    wt, gpu = backend_for("compressed_sr", 0, False)
+    x = wl.adjust(wl.make_input("compressed-x4"), wt)
+    out, aux = gpu.handle.forward_batch(x)
+    assert out.shape == (256, 3, 192, 192) and aux.shape == (256, 3, 56, 56)
+    O = oracle()
+    for i in range(0, 256, 17):
+        ref, raux = O.forward(wt, 48, 48, x[i])
+        check(out[i], ref, f"compressed-x4 member {i}")
+        check(aux[i], raux, f"compressed-x4 member {i} aux")
+        one, one_aux = gpu.handle.forward_batch(x[i:i + 1])
+        assert np.array_equal(one[0], out[i]) and np.array_equal(one_aux[0], aux[i]), i
+
+
+@pytest.mark.parametrize("task,h,w", [("classical_sr", 40, 56), ("real_sr", 24, 40)])
+def test_two_term_operands_on_the_wide_network(task, h, w, monkeypatch):
+    """S2S_SPLIT=1 (read at create) gives the 180-wide network the two-term operands
+    the 60-wide one runs on (hi + lo fp16 through every GEMM, conv and the attention's
+    products): its output stays within the gate and moves closer to the oracle than
+    the single-term forward's."""
+    O = oracle()
+    capi = importlib.import_module("swin2sr_b200.capi")
+    P = pkg()
+    wt = P.weights.Weights.seeded(task, 0, True)
+    x = adjust(wt, np.random.default_rng(h * 7 + w).random((1, 3, h, w), dtype=np.float32))
+    ref, _ = O.forward(wt, h, w, x[0])
+    H = capi.Handle(wt)
+    try:
+        single = H.forward_batch(x)[0][0]
+    finally:
+        H.close()
+    monkeypatch.setenv("S2S_SPLIT", "1")
+    H = capi.Handle(wt)
+    try:
+        two = H.forward_batch(x)[0][0]
+    finally:
+        H.close()
+    e1 = check(single, ref, f"{task} single-term")
+    e2 = check(two, ref, f"{task} two-term")
+    assert e2 < e1, (e2, e1)
 
 
 @pytest.mark.parametrize("task", ["classical_sr", "compressed_sr"])
@@ -317,5 +375,5 @@ def test_selftest_runs_every_consistency_check(task):
     print(rep)
     assert rc == capi.S2S_OK, rep
     for name in ("batch_vs_single", "graph_replay_vs_eager", "patches_vs_tap_boxes",
-                 "fused_vs_unfused_mlp"):
+                 "fused_vs_unfused_mlp", "two_term_vs_single_term"):
         assert f"{name} ok" in rep, rep
