@@ -62,7 +62,7 @@ class Gpu(Backend):
         return g
 
     def name(self) -> str:
-        return "gpu"
+        return "cuda"  # src/gpu.rs:737-739; --verify prints it (src/main.rs:692)
 
     def forward(self, h: int, w: int, inp: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(inp, dtype=np.float32).reshape(1, 3, h, w)
@@ -162,10 +162,13 @@ def is_out_of_memory(err: Exception) -> bool:
 
 
 def run_with_fallback(wt, backend: Backend, img: np.ndarray, tile: int, pad: int,
-                      note=None):
+                      note=None, note_exact=None):
     """src/main.rs:579-657: run_tiled, halving the tile on out-of-memory (a failed
     whole-image pass falls back to half the image), down to one window.
-    Returns (image, the tile that ran). `note` receives each retry's message."""
+    Returns (image, the tile that ran). `note` receives each retry's message; a retry
+    out of the whole-image pass (tile 0, the only exact mode) goes to `note_exact`
+    instead when given, since the reference announces that one even under -q
+    (src/main.rs:627-640)."""
     for _ in range(64):
         try:
             return run_tiled(wt, backend, img, tile, pad), tile
@@ -181,7 +184,15 @@ def run_with_fallback(wt, backend: Backend, img: np.ndarray, tile: int, pad: int
             if not shrinking or nxt == 0:
                 raise RuntimeError(f"{e}\n(a {wt.window}-pixel tile is the smallest this engine "
                                    f"will run, and it did not fit either)") from e
-            if note:
-                note(f"{e} - retrying with a {nxt}x{nxt} tile")
+            if tile == 0:
+                msg = (f"{str(e).rstrip('.')} - retrying with a {nxt}x{nxt} tile (--tile 0 is "
+                       f"the only exact mode; this run is now tiled, and tiled results differ "
+                       f"slightly from one pass)")
+                sink = note_exact or note
+            else:
+                msg = f"{str(e).rstrip('.')} - retrying with a {nxt}x{nxt} tile"
+                sink = note
+            if sink:
+                sink(msg)
             tile = nxt
     raise RuntimeError(f"gave up after 64 tile reductions at tile {tile}")

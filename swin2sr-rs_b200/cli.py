@@ -62,11 +62,16 @@ def plan_batches(headers, batch: int):
 
 
 def upscale_pngs(handles, pngs, batch: int = 8, level: int = -1, threads: int = 0,
-                 want_aux: bool = False, stats: dict | None = None):
+                 want_aux: bool = False, stats: dict | None = None, pad: int = 32,
+                 note=None, note_exact=None):
     """PNG bytes in -> PNG bytes out (and aux PNGs, or None each), in input order.
 
     `handles` are capi.Handle objects, one per device; batches are spread over them.
-    `threads` sizes the host pool (0 = all cores)."""
+    `threads` sizes the host pool (0 = all cores). A batch whose whole-image pass runs
+    out of device memory is redone image by image through the tiled driver from tile 0
+    (run_with_fallback: the whole image alone, then halving tiles with `pad` context),
+    as the reference's --tile 0 retries (src/main.rs:579-657); its aux is then None."""
+    from . import backend, image
     if not handles:
         raise ValueError("at least one handle")
     wt = handles[0].wt
@@ -101,7 +106,21 @@ def upscale_pngs(handles, pngs, batch: int = 8, level: int = -1, threads: int = 
                 try:
                     _, _, _, depth = key
                     samples = np.stack([dec_f[i].result()[0] for i in idx])
-                    rows, arows = H.forward_image(samples, depth, png_rows=True)
+                    try:
+                        rows, arows = H.forward_image(samples, depth, png_rows=True)
+                    except capi.S2SError as e:
+                        if not backend.is_out_of_memory(e):
+                            raise
+                        gpu = backend.Gpu.from_handle(H)
+                        for i in idx:
+                            img = image.samples_to_image(dec_f[i].result()[0], depth)
+                            res, _ = backend.run_with_fallback(wt, gpu, img.data, 0, pad, note,
+                                                               note_exact)
+                            rgb = image.Image(img.w * wt.scale, img.h * wt.scale, res).to_rgb8()
+                            with lock:
+                                enc_f.append((i, False, pool.submit(
+                                    capi.png_encode_rgb8, rgb, level, enc_threads)))
+                        continue
                     with lock:
                         for k, i in enumerate(idx):
                             enc_f.append((i, False, pool.submit(
@@ -134,7 +153,7 @@ def upscale_pngs(handles, pngs, batch: int = 8, level: int = -1, threads: int = 
 
 
 def upscale_pngs_tiled(handles, pngs, tile: int, pad: int, level: int = -1, threads: int = 0,
-                       note=None, stats: dict | None = None):
+                       note=None, stats: dict | None = None, note_exact=None):
     """PNG bytes in -> PNG bytes out through the tiled driver, images spread over the
     handles (one host thread each). Returns (outputs, the tile each image ran with)."""
     from . import backend, image
@@ -153,7 +172,8 @@ def upscale_pngs_tiled(handles, pngs, tile: int, pad: int, level: int = -1, thre
             try:
                 samples, depth = capi.png_decode(pngs[i])
                 img = image.samples_to_image(samples, depth)
-                res, ran[i] = backend.run_with_fallback(wt, gpu, img.data, tile, pad, note)
+                res, ran[i] = backend.run_with_fallback(wt, gpu, img.data, tile, pad, note,
+                                                        note_exact)
                 rgb = image.Image(img.w * wt.scale, img.h * wt.scale, res).to_rgb8()
                 out[i] = capi.png_encode_rgb8(rgb, level, threads)
             except Exception as e:  # noqa: BLE001 - reported after the join
@@ -229,14 +249,17 @@ def main(argv=None) -> int:
     handles = [capi.Handle(wt, int(d)) for d in a.devices.split(",")]
     try:
         stats: dict = {}
+        # retry notes take -q, except a whole-image pass falling back to tiles: that run
+        # is no longer the exact one asked for, so it is announced regardless
+        say = lambda m: print(f"note: {m}", file=sys.stderr)  # noqa: E731
+        note = None if a.quiet else say
         if tiled:
-            note = None if a.quiet else (lambda m: print(f"  {m}", file=sys.stderr))
             outs, _ = upscale_pngs_tiled(handles, pngs, tile, a.tile_pad, a.level, a.threads,
-                                         note, stats)
+                                         note, stats, note_exact=say)
             auxs = [None] * len(outs)
         else:
             outs, auxs = upscale_pngs(handles, pngs, a.batch, a.level, a.threads, bool(a.aux),
-                                      stats)
+                                      stats, a.tile_pad, note, say)
     except (capi.S2SError, RuntimeError) as e:
         print(f"error: {e}", file=sys.stderr)
         return 1

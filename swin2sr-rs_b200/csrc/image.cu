@@ -223,7 +223,16 @@ struct Png {
   int depth = 0, ctype = 0, interlace = 0;
   int channels = 0;
   std::vector<uint8_t> idat;
+  uint64_t idat_bytes = 0;  // summed IDAT chunk lengths
 };
+
+// Deflate codes at most 258 bytes of output per 2 bits of input: a zlib stream of n
+// bytes inflates to less than 1032 (n + 1) bytes.
+constexpr uint64_t kMaxInflateRatio = 1032;
+
+// The filtered (with filter-type bytes) size of the image: one run per row, or per
+// row of each Adam7 pass.
+uint64_t raw_bytes(const Png& p);
 
 uint32_t be32(const uint8_t* p) {
   return (uint32_t)p[0] << 24 | (uint32_t)p[1] << 16 | (uint32_t)p[2] << 8 | p[3];
@@ -245,9 +254,11 @@ const char* depth_name(int d) {
   }
 }
 
-// Parse the chunk stream. `want_data` false stops after IHDR. Error messages for
-// the two refusals follow src/image.rs:55-65, which formats the png crate's
-// ColorType / BitDepth with {:?}.
+// Parse the chunk stream. `want_data` false (a header query) checks only IHDR, then
+// sums the IDAT chunk lengths of whatever complete chunks follow, so that a header
+// whose dimensions the image data cannot possibly fill is refused before any caller
+// sizes a buffer from it. Error messages for the two refusals follow
+// src/image.rs:55-65, which formats the png crate's ColorType / BitDepth with {:?}.
 Png parse_png(const uint8_t* d, size_t n, bool want_data) {
   if (!d || n < 8 || memcmp(d, kSig, 8) != 0) fail(S2S_ERR_INVALID, "not a PNG file (bad signature)");
   Png p;
@@ -255,11 +266,19 @@ Png parse_png(const uint8_t* d, size_t n, bool want_data) {
   bool have_ihdr = false, done = false;
   while (!done) {
     if (n - off < 12) {
-      if (have_ihdr && want_data && !p.idat.empty()) break;  // no IEND: decode what is there
+      if (have_ihdr && (!want_data || !p.idat.empty())) break;  // no IEND: what is there
       fail(S2S_ERR_INVALID, "truncated PNG chunk stream");
     }
     const uint32_t len = be32(d + off);
     const uint8_t* type = d + off + 4;
+    if (have_ihdr && !want_data) {
+      // header query: the rest is only measured (no CRC, no copy); a cut ends it
+      if (len > 0x7fffffffu || (size_t)len > n - off - 12) break;
+      if (memcmp(type, "IDAT", 4) == 0) p.idat_bytes += len;
+      if (memcmp(type, "IEND", 4) == 0) break;
+      off += 12 + (size_t)len;
+      continue;
+    }
     if (len > 0x7fffffffu || (size_t)len > n - off - 12) fail(S2S_ERR_INVALID, "truncated PNG chunk");
     const uint8_t* body = d + off + 8;
     const uint32_t crc = be32(body + len);
@@ -288,9 +307,9 @@ Png parse_png(const uint8_t* d, size_t n, bool want_data) {
       p.channels = p.ctype == 0 ? 1 : p.ctype == 4 ? 2 : p.ctype == 2 ? 3 : 4;
       if (p.depth < 8) fail(S2S_ERR_INVALID, std::string("unsupported png bit depth ") + depth_name(p.depth));
       have_ihdr = true;
-      if (!want_data) return p;
     } else if (memcmp(type, "IDAT", 4) == 0) {
       p.idat.insert(p.idat.end(), body, body + len);
+      p.idat_bytes += len;
     } else if (memcmp(type, "IEND", 4) == 0) {
       done = true;
     } else if (!(type[0] & 0x20)) {
@@ -300,7 +319,10 @@ Png parse_png(const uint8_t* d, size_t n, bool want_data) {
     }
     off += 12 + (size_t)len;
   }
-  if (p.idat.empty()) fail(S2S_ERR_INVALID, "PNG has no image data");
+  if (want_data && p.idat.empty()) fail(S2S_ERR_INVALID, "PNG has no image data");
+  // image data that cannot inflate to the image (only judged once some was seen)
+  if (p.idat_bytes > 0 && raw_bytes(p) > kMaxInflateRatio * (p.idat_bytes + 1))
+    fail(S2S_ERR_INVALID, "truncated PNG image data");
   return p;
 }
 
@@ -347,18 +369,21 @@ void unfilter(int ft, uint8_t* row, const uint8_t* prev, size_t len, int bpp) {
 
 // Inflate + unfilter (+ de-interlace) into interleaved samples, big-endian for 16
 // bits: the buffer the png crate's next_frame fills (src/image.rs:50-52).
+uint64_t raw_bytes(const Png& p) {
+  const uint64_t bpp = (uint64_t)p.channels * p.depth / 8;
+  if (!p.interlace) return (uint64_t)p.h * ((uint64_t)p.w * bpp + 1);
+  uint64_t n = 0;
+  for (const Pass& q : kAdam7) {
+    const uint64_t pw = pass_len(p.w, q.x0, q.dx), ph = pass_len(p.h, q.y0, q.dy);
+    if (pw && ph) n += ph * (pw * bpp + 1);
+  }
+  return n;
+}
+
 void decode_png(const Png& p, uint8_t* out) {
   const int bpp = p.channels * p.depth / 8;
   const size_t row_bytes = (size_t)p.w * bpp;
-  size_t raw_n = 0;
-  if (!p.interlace) {
-    raw_n = (size_t)p.h * (row_bytes + 1);
-  } else {
-    for (const Pass& q : kAdam7) {
-      const size_t pw = pass_len(p.w, q.x0, q.dx), ph = pass_len(p.h, q.y0, q.dy);
-      if (pw && ph) raw_n += ph * (pw * bpp + 1);
-    }
-  }
+  const size_t raw_n = (size_t)raw_bytes(p);
   std::vector<uint8_t> raw(raw_n);
   z_stream z{};
   if (inflateInit(&z) != Z_OK) fail(S2S_ERR_INVALID, "inflateInit failed");

@@ -478,7 +478,8 @@ def test_decoder_survives_corrupt_and_hostile_files():
         with pytest.raises(C.S2SError):
             C.png_decode(base[:cut])
     assert np.array_equal(C.png_decode(base[:last_idat_end])[0].reshape(13, 44), rows)
-    for w, h in [(1 << 31 - 1, 1 << 31 - 1), (1 << 20, 1 << 20), (0, 5), (5, 0)]:
+    for w, h in [((1 << 31) - 1, (1 << 31) - 1), (1 << 20, 1 << 20), (1 << 17, (1 << 17) + 1),
+                 (0, 5), (5, 0)]:
         ihdr = struct.pack(">IIBBBBB", w, h, 8, 6, 0, 0, 0)
         f = b"\x89PNG\r\n\x1a\n" + chunk(b"IHDR", ihdr) + chunk(b"IDAT", zlib.compress(b"\0" * 64)) \
             + chunk(b"IEND", b"")
@@ -486,6 +487,22 @@ def test_decoder_survives_corrupt_and_hostile_files():
             C.png_header(f)
         L = C.load()
         assert L.s2s_png_decode(f, len(f), None, 0) == C.S2S_ERR_INVALID
+    # exactly 2^34 pixels passes the dimension check, but 16-bit RGBA of that size
+    # (128 GiB of filtered rows) cannot come out of a tiny zlib stream: the header query
+    # refuses it, so no caller sizes a sample buffer from it (png_decode would
+    # otherwise allocate the output before the decoder runs)
+    for depth, ctype in [(16, 6), (8, 0)]:
+        ihdr = struct.pack(">IIBBBBB", 1 << 17, 1 << 17, depth, ctype, 0, 0, 0)
+        f = b"\x89PNG\r\n\x1a\n" + chunk(b"IHDR", ihdr) + chunk(b"IDAT", zlib.compress(b"\0" * 64)) \
+            + chunk(b"IEND", b"")
+        with pytest.raises(C.S2SError, match="truncated PNG image data"):
+            C.png_header(f)
+        with pytest.raises(C.S2SError, match="truncated PNG image data"):
+            C.png_decode(f)
+        assert L.s2s_png_decode(f, len(f), None, 0) == C.S2S_ERR_INVALID
+    # a header-only prefix (no image data yet) still answers the header query
+    ihdr = struct.pack(">IIBBBBB", 1 << 17, 1 << 17, 8, 2, 0, 0, 0)
+    assert C.png_header(b"\x89PNG\r\n\x1a\n" + chunk(b"IHDR", ihdr)) == (1 << 17, 1 << 17, 3, 8)
 
 
 class _FakeFloatHandle:
@@ -533,6 +550,38 @@ def test_tiled_cli_path_matches_the_whole_image_and_recovers_from_oom():
     assert ran == [24] and len(notes) == 1 and "retrying with a 24x24 tile" in notes[0]
     assert np.array_equal(np.array(PILImage.open(io.BytesIO(outs[0]))), want[0])
     assert max(a * b for a, b in h.sizes[1:]) <= 40 * 40
+
+
+class _FakeImageHandle(_FakeFloatHandle):
+    """The batched (whole-image) CLI path's handle: its image forward runs out of
+    memory, as a batch too large for the device would."""
+
+    def forward_image(self, samples, depth, png_rows=True):
+        capi_mod = cli_mod().capi
+        raise capi_mod.S2SError(capi_mod.S2S_ERR_OOM,
+                                "cudaMalloc: CUDA_ERROR_OUT_OF_MEMORY (fake)")
+
+
+def test_whole_image_cli_path_falls_back_to_tiles_and_says_so_under_quiet():
+    """--tile 0 (the default, batched path): a batch that runs out of device memory is
+    redone image by image from tile 0 - the whole image alone, then halving tiles - as
+    the reference retries (src/main.rs:579-657). The note for leaving the exact
+    whole-image mode goes to note_exact, which the CLI prints even under -q."""
+    cli = cli_mod()
+    P = pkg()
+    wt = P.weights.Weights.seeded("classical_sr", 0)
+    imgs = [smooth_rgb(40, 56, 1), smooth_rgb(33, 20, 2)]
+    pngs = [pil_png(a, "RGB") for a in imgs]
+    want = [np.array(a).repeat(4, axis=0).repeat(4, axis=1) for a in imgs]
+    exact = []
+    outs, aux = cli.upscale_pngs([_FakeImageHandle(wt, limit=40 * 40)], pngs, batch=2, pad=8,
+                                 note=None, note_exact=exact.append)
+    for o, w_ in zip(outs, want):
+        assert np.array_equal(np.array(PILImage.open(io.BytesIO(o))), w_)
+    assert aux == [None, None]
+    # only the 40x56 image needs tiles (33x20 fits whole)
+    assert len(exact) == 1 and "--tile 0 is the only exact mode" in exact[0]
+    assert "retrying with a 24x24 tile" in exact[0]
 
 
 def test_cli_refuses_aux_with_tiling(tmp_path, capsys):
