@@ -2,13 +2,15 @@
  *
  * This is the boundary the reference's GPU backend plugs into: swin2sr-rs
  * src/gpu.rs implements `Backend` (src/backend.rs:29-49) for `Gpu`; a drop-in
- * `Gpu` keeps that trait impl and forwards to these entry points (the binding a
- * maintainer adds is in INTEGRATION.md). Plain C types only; every pointer is
- * caller-owned unless stated.
+ * `Gpu` keeps that trait impl and forwards to these entry points through an FFI
+ * binding. Plain C types only; every pointer is caller-owned unless stated.
  *
  * Threading: a handle is not thread-safe (the reference's `forward` takes
  * `&mut self`); one CUDA stream per handle; the host-buffer calls return when the
- * result is on the host.
+ * result is on the host. Calls on one handle from several threads (only the
+ * allocation-free attention entry point below invites that) share its kernel
+ * launch counter, which is atomic, and its last-error string, which holds the
+ * message of whichever call failed last.
  */
 #ifndef S2S_H
 #define S2S_H
@@ -189,7 +191,8 @@ int s2s_band_halo_ops(int rank, int world, int own_rows, int rows, int cyclic, i
  * holding S2S_NOALLOC_MAX_TOKENS rows (4 MiB); batch * hp * wp above that is
  * rejected with S2S_ERR_INVALID. d_qkv is [batch*hp*wp][3*heads*dp] fp16 in image
  * order, per token [head][q|k|v][dp] with dp = head_dim rounded up to 16 (16-byte
- * aligned), as the forward's QKV projection writes it: q and k L2-normalised, q
+ * aligned), the single-term layout the forward's QKV GEMM writes (S2S_ATTN=mma and
+ * S2S_SPLIT=0 make a forward use that GEMM): q and k L2-normalised, q
  * times exp(min(logit_scale, ln 100)) * log2(e); d_out is [batch*hp*wp][ld_out] fp16, of which columns [0, embed) are
  * written. hp and wp are the padded plane (multiples of the window); odd blocks
  * use the shifted window grid. Work is enqueued on `stream` (NULL = the handle's

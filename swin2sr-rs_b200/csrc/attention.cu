@@ -63,26 +63,6 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// 2^x by the SFU: PTX ex2.approx (the logits are pre-scaled by log2 e).
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ int region_of(int a, int p, int win, int shift) {
-  return (a + win < p) ? 0 : (a + shift < p) ? 1 : 2;
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
-                                         uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // DP: padded head dim (16 or 32); HPC heads per CTA; SPLIT: two-term operands.
 // Window of 64 tokens (win = 8). row_h: halves per QKV token row.
 template <int DP, int HPC, bool SPLIT>

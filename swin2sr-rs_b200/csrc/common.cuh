@@ -145,6 +145,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t phase) {
   return ok != 0;
 }
 
+// Non-blocking test: has the phase with parity `phase` completed? (Only meaningful
+// when the caller knows the barrier is at most one phase ahead of that one.)
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the barrier's phase `phase` to complete, for at most ~2 s of wall time.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, unsigned code) {
   const uint32_t a = smem_u32(bar);
@@ -226,6 +240,31 @@ __device__ __forceinline__ void bulk_wait() {
 // (TMA / tensor core) accesses.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- attention helpers
+// 2^x by the SFU: PTX ex2.approx (the attention logits are pre-scaled by log2 e).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Shift-mask region of rolled-plane coordinate a along an axis of p pixels
+// (src/plan.rs:80-108): 0 before the last window, 1 in it before the shift, 2 after.
+__device__ __forceinline__ int region_of(int a, int p, int win, int shift) {
+  return (a + win < p) ? 0 : (a + shift < p) ? 1 : 2;
+}
+
+// One bulk copy global -> shared (16-byte aligned, a multiple of 16 bytes),
+// completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 // ---------------------------------------------------------------- GELU
@@ -376,6 +415,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   tc_wait_ld();
 #pragma unroll
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// The same load without the wait: issue several, then tc_wait_ld() once.
+__device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
 }
 
 // Shared-memory matrix descriptor for a K-major tile in the 128-byte swizzle

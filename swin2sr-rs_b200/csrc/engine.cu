@@ -65,9 +65,12 @@ thread_local std::string g_create_error;
 // s2s_selftest creates its comparison handles with these settings of the validation
 // switches (-1: as the environment says).
 struct CreateFlags {
-  int unfused_mlp = -1, no_patch = -1, split = -1;
+  int unfused_mlp = -1, no_patch = -1, split = -1, mma_attn = -1;
 };
 thread_local CreateFlags g_create_flags;
+
+// Whether 180-wide handles run QKV + attention as the one fused kernel by default.
+constexpr bool kFusedAttnDefault = true;
 
 struct S2SError {
   int code;
@@ -98,6 +101,11 @@ struct Block {
   TcWeight qkv, proj, fc1, fc2;
   float *n1g, *n1b, *n2g, *n2b;
   float *cpb, *ls;  // bias table and q scale, both times log2 e (attention softmax is exp2)
+  // the fused QKV + attention kernel's operands: Wqkv [6 x 96][Cp] (per head q, k, v
+  // rows of 32), q and v biases [6][32], and the compact [6][576] position-bias table
+  // (times log2 e)
+  TcWeight wqkv;
+  float *qb = nullptr, *vb = nullptr, *cpbc = nullptr;
 };
 
 struct Stage {
@@ -141,6 +149,7 @@ struct Plan {
   float *BIC = nullptr, *BICF = nullptr, *AUXRAW = nullptr;
   int* rows[2] = {nullptr, nullptr};  // window-major token -> image row, shift 0 / win/2
   CUtensorMap mF0h, mX16, mAO, mH16, cX16, cAO, cHA;
+  CUtensorMap mXw;  // X16 plane in 4 x 4-pixel boxes (the fused attention's windows)
   CUtensorMap cHB[3][3];  // head planes at 1x, 2x, 4x resolution
   CUtensorMap cHBp[3][3];                 // the same planes in (boxh + 2)-row patches
   bool hbp[3][3] = {{false}};             // ... when the plane's conv box allows them
@@ -168,6 +177,11 @@ struct s2s_handle {
   // Cs, NQs, HIDs: row strides (halves) of the X16/AO/F0h, QKV and H16 buffers.
   bool split = false;
   int Cs = 0, NQs = 0, HIDs = 0;
+  // QKV projection and window attention in one tcgen05 kernel (k_qkv_attention) for
+  // 6 heads of 32 (padded) over Cp = 192; AO rows are then [head][32] and the proj
+  // weights' K follows that order. S2S_ATTN=mma / fused (validation switch): the QKV
+  // GEMM + mma.sync attention kernel pair, or the fused kernel.
+  bool fused_attn = false;
   float* cf_w = nullptr;
   float* cf_b = nullptr;
   TcWeight pe;
@@ -403,13 +417,39 @@ void build_weights(s2s_handle* H, const TensorTable& T, std::vector<void*>& tmp)
         b3[i] = qb[i];
         b3[2 * C + i] = vb[i];
       }
-      std::vector<int> qmap(H->NQ, -1);
-      for (int part = 0; part < 3; part++)
+      if (!H->fused_attn) {
+        std::vector<int> qmap(H->NQ, -1);
+        for (int part = 0; part < 3; part++)
+          for (int h = 0; h < heads; h++)
+            for (int d = 0; d < hd; d++) qmap[(h * 3 + part) * DP + d] = part * C + h * hd + d;
+        pack_linear(H, bl.qkv, W3.data(), b3.data(), C, H->NQ, Cp, n_tile_for(H->NQ), qmap, sp);
+        pack_linear(H, bl.proj, T.get(p + "attn.proj.weight", (int64_t)C * C),
+                    T.get(p + "attn.proj.bias", C), C, Cp, Cp, Cp, identity_rows(Cp, C), sp);
+      } else {
+        // fused kernel: head h's q, k, v rows at h * 96, + 32, + 64 (head_dim padded to 32)
+        std::vector<int> mqkv(heads * 96, -1);
+        std::vector<float> qbp(heads * 32, 0.0f), vbp(heads * 32, 0.0f);
         for (int h = 0; h < heads; h++)
-          for (int d = 0; d < hd; d++) qmap[(h * 3 + part) * DP + d] = part * C + h * hd + d;
-      pack_linear(H, bl.qkv, W3.data(), b3.data(), C, H->NQ, Cp, n_tile_for(H->NQ), qmap, sp);
-      pack_linear(H, bl.proj, T.get(p + "attn.proj.weight", (int64_t)C * C),
-                  T.get(p + "attn.proj.bias", C), C, Cp, Cp, Cp, identity_rows(Cp, C), sp);
+          for (int d = 0; d < hd; d++) {
+            mqkv[h * 96 + d] = h * hd + d;
+            mqkv[h * 96 + 32 + d] = C + h * hd + d;
+            mqkv[h * 96 + 64 + d] = 2 * C + h * hd + d;
+            qbp[h * 32 + d] = qb[h * hd + d];
+            vbp[h * 32 + d] = vb[h * hd + d];
+          }
+        pack_linear(H, bl.wqkv, W3.data(), nullptr, C, heads * 96, Cp, 192, mqkv);
+        bl.qb = upload(H, qbp);
+        bl.vb = upload(H, vbp);
+        // proj reads AO as [head][32]: K index h * 32 + d <- input channel h * hd + d
+        const float* pw = T.get(p + "attn.proj.weight", (int64_t)C * C);
+        std::vector<float> pwr((size_t)C * Cp, 0.0f);
+        for (int o = 0; o < C; o++)
+          for (int h = 0; h < heads; h++)
+            for (int d = 0; d < hd; d++)
+              pwr[(size_t)o * Cp + h * 32 + d] = pw[(size_t)o * C + h * hd + d];
+        pack_linear(H, bl.proj, pwr.data(), T.get(p + "attn.proj.bias", C), Cp, Cp, Cp, Cp,
+                    identity_rows(Cp, C));
+      }
       pack_linear(H, bl.fc1, T.get(p + "mlp.fc1.weight", (int64_t)HID * C),
                   T.get(p + "mlp.fc1.bias", HID), C, HIDp, Cp, n_tile_for(HIDp),
                   identity_rows(HIDp, HID), sp);
@@ -437,8 +477,25 @@ void build_weights(s2s_handle* H, const TensorTable& T, std::vector<void*>& tmp)
               cpbt[((size_t)h * n + q) * n + (k ^ ((q & 7) << 2))] =
                   cpb[((size_t)q * n + k) * heads + h] * kLog2e;
         bl.cpb = upload(H, cpbt);
+        if (H->fused_attn) {
+          // compact table: entry 40 (dy + 7) + dx + 7 for query - key = (dy, dx)
+          std::vector<float> cc((size_t)heads * 576, 0.0f);
+          for (int dy = -7; dy <= 7; dy++)
+            for (int dx = -7; dx <= 7; dx++) {
+              const int qy = std::max(dy, 0), qx = std::max(dx, 0);
+              const int qi = qy * 8 + qx, ki = (qy - dy) * 8 + (qx - dx);
+              for (int h = 0; h < heads; h++)
+                cc[(size_t)h * 576 + 40 * (dy + 7) + dx + 7] =
+                    cpb[((size_t)qi * n + ki) * heads + h] * kLog2e;
+            }
+          bl.cpbc = upload(H, cc);
+        }
       } else {
         bl.cpb = cpb_from_mlp(H, T, p, heads, tmp);
+        if (H->fused_attn) {
+          bl.cpbc = upload(H, std::vector<float>((size_t)heads * 576, 0.0f));
+          ck(launch_cpb_compact(bl.cpb, bl.cpbc, heads, 0), "cpb compact table");
+        }
       }
       const float* ls = T.get(p + "attn.logit_scale", heads);
       std::vector<float> lse(heads);
@@ -545,7 +602,7 @@ int64_t plan_bytes(const s2s_handle* H, int B, int h, int w) {
   b += (int64_t)B * 3 * hp * wp * 4;        // P
   b += 3 * T * Cp * 4;                      // F0, X, S
   b += 3 * T * H->Cs * 2;                   // F0h, X16, AO
-  b += T * H->NQs * 2 + (H->fused_mlp ? 0 : T * H->HIDs * 2);  // QKV, H16 (unfused MLP)
+  b += (H->fused_attn ? 0 : T * H->NQs * 2) + (H->fused_mlp ? 0 : T * H->HIDs * 2);  // QKV, H16
   b += 2 * T * 4;                           // window row tables
   b += T * 64 * 2 + 3 * T * s * s * 64 * 2; // head planes
   if (H->cfg.upsampler == S2S_PIXELSHUFFLE_AUX)
@@ -634,7 +691,7 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
     P->F0h = (__half*)dalloc(*P, T * Cs * 2);
     P->X16 = (__half*)dalloc(*P, T * Cs * 2);
     P->AO = (__half*)dalloc(*P, T * Cs * 2);
-    P->QKV = (__half*)dalloc(*P, T * H->NQs * 2);
+    if (!H->fused_attn) P->QKV = (__half*)dalloc(*P, T * H->NQs * 2);
     if (!H->fused_mlp) P->H16 = (__half*)dalloc(*P, T * H->HIDs * 2);
     for (int i = 0; i < 2; i++) P->rows[i] = (int*)dalloc(*P, (size_t)P->nwin[i] * 64 * 4);
     P->HA = (__half*)dalloc(*P, Th * 64 * 2);
@@ -699,6 +756,7 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
     ok &= make_map_nhwc(&P->cAO, P->AO + (size_t)P->head_row0 * wp * Cs, B, P->head_rows, wp, Cs,
                         bw, bh);
     ok &= make_map_nhwc(&P->cHA, P->HA, B, P->head_rows, wp, 64, bw, bh);
+    if (H->fused_attn) ok &= make_map_nhwc(&P->mXw, P->X16, B, hp, wp, Cs, 4, 4);
   }
   for (int i = 0; i < 3; i++)
     for (int r = 0; r < 3; r++) {
@@ -1007,7 +1065,37 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         two_term(a, sp);
         L.run("gemm_qkv", [&] { return launch_gemm(mA, bl.qkv.map, out_maps(P, a), a, bl.qkv.BN, st); });
       };
-      if (band && sh) {
+      if (H->fused_attn) {
+        // QKV projection + attention in one kernel; the shifted windows' 4 rows from each
+        // neighbouring band (cyclically) arrive first
+        if (band && sh) exchange("halo_shift", P->X16, 4, true, false);
+        QaArgs qa;
+        memset(&qa, 0, sizeof qa);
+        qa.out = P->AO;
+        qa.ld_out = Cs;
+        qa.qb = bl.qb;
+        qa.vb = bl.vb;
+        qa.ls = bl.ls;
+        qa.bias = bl.cpbc;
+        qa.nww = wp / 8;
+        qa.wp = wp;
+        qa.hp_l = hp;
+        qa.ghp = P->ghp;
+        qa.y_mod = hp;
+        qa.shift = sh;
+        if (!band) {
+          qa.B = B;
+          qa.nw_img = (hp / 8) * (wp / 8);
+          qa.y_base = sh;
+        } else {
+          qa.B = 1;
+          qa.nw_img = P->nwin[k];
+          qa.y_base = P->halo - sh;
+          qa.wh_off = P->wh_off[k];
+        }
+        qa.nwin_total = P->nwin[k];
+        L.run("qkv_attention", [&] { return launch_qkv_attention(P->mXw, bl.wqkv.map, qa, st); });
+      } else if (band && sh) {
         // The shifted windows reach 4 rows into each neighbouring band (cyclically).
         // Those rows travel on the side stream while the owned rows' QKV runs; the
         // halo rows' QKV follows their arrival.
@@ -1023,11 +1111,12 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
       } else {
         qkv(P->mX16, P->own_off, M);
       }
-      L.run("window_attention", [&] {
-        return launch_window_attention(P->QKV, P->AO, bl.cpb, P->rows[k], P->nwin[k],
-                                       H->heads, H->hd, H->DP, Cs, H->NQs, sp, H->NQ, lo,
-                                       P->nwh_l[k], wp / 8, P->ghp, wp, sh, P->wh_off[k], st);
-      });
+      if (!H->fused_attn)
+        L.run("window_attention", [&] {
+          return launch_window_attention(P->QKV, P->AO, bl.cpb, P->rows[k], P->nwin[k],
+                                         H->heads, H->hd, H->DP, Cs, H->NQs, sp, H->NQ, lo,
+                                         P->nwh_l[k], wp / 8, P->ghp, wp, sh, P->wh_off[k], st);
+        });
       {  // proj + norm1 + residual, in place
         Epi e = epi0();
         e.bias = bl.proj.b;
@@ -1523,6 +1612,14 @@ int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, 
   H->Cs = H->split ? 2 * H->Cp : H->Cp;
   H->NQs = H->split ? 2 * H->NQ : H->NQ;
   H->HIDs = H->split ? 2 * H->HIDp : H->HIDp;
+  const bool can_fuse_attn = !H->split && H->Cp == 192 && H->heads == 6 && H->DP == 32;
+  H->fused_attn = can_fuse_attn && kFusedAttnDefault;
+  {
+    const char* v = getenv("S2S_ATTN");
+    if (v && strcmp(v, "mma") == 0) H->fused_attn = false;
+    if (v && strcmp(v, "fused") == 0) H->fused_attn = can_fuse_attn;
+    if (g_create_flags.mma_attn >= 0) H->fused_attn = can_fuse_attn && !g_create_flags.mma_attn;
+  }
   // the fused MLP keeps its hidden activation in single-term fp16
   const bool can_fuse = !H->split && ((H->Cp == 192 && H->HIDp == 384) ||
                                       (H->Cp == 64 && H->HIDp == 128));
@@ -1851,7 +1948,7 @@ int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors
   std::string rep;
   bool all_ok = true;
   int status = S2S_OK;
-  s2s_handle* hs[4] = {nullptr, nullptr, nullptr, nullptr};
+  s2s_handle* hs[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   auto check = [&](const char* name, double err, double tol) {
     char b[192];
     const bool ok = err <= tol;
@@ -1862,10 +1959,12 @@ int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors
   };
   // handle k with the given validation switches; false (and the error in the report)
   // when it cannot be made
-  auto make = [&](int k, int unfused_mlp, int no_patch, int split = -1) -> bool {
+  auto make = [&](int k, int unfused_mlp, int no_patch, int split = -1,
+                  int mma_attn = -1) -> bool {
     g_create_flags.unfused_mlp = unfused_mlp;
     g_create_flags.no_patch = no_patch;
     g_create_flags.split = split;
+    g_create_flags.mma_attn = mma_attn;
     const int rc = s2s_create(cfg, tensors, n_tensors, device, &hs[k]);
     g_create_flags = CreateFlags{};
     if (rc != S2S_OK) {
@@ -1925,6 +2024,13 @@ int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors
   go = go && make(3, 1, 0, hs[0]->split ? 0 : 1) &&
        ran(hs[3], s2s_forward(hs[3], h, w, in.data(), other.data(), nullptr), "forward");
   if (go) check("two_term_vs_single_term", maxabs(other.data(), eager.data(), nout), 2e-2);
+  // the fused QKV + attention kernel against the QKV GEMM + mma.sync attention pair (the
+  // other of the two for this handle)
+  if (go && !hs[0]->split && hs[0]->Cp == 192 && hs[0]->heads == 6 && hs[0]->DP == 32) {
+    go = make(4, 0, 0, -1, hs[0]->fused_attn ? 1 : 0) &&
+         ran(hs[4], s2s_forward(hs[4], h, w, in.data(), other.data(), nullptr), "forward");
+    if (go) check("fused_vs_unfused_attention", maxabs(other.data(), eager.data(), nout), 2e-3);
+  }
   for (s2s_handle*& x : hs)
     if (x) s2s_destroy(x);
   if (report && cap > 0) {

@@ -117,6 +117,33 @@ cudaError_t launch_mlp(const CUtensorMap& mapX, const CUtensorMap& mapW1,
                        const CUtensorMap& mapX16o, const MlpArgs& a, int cp, int hp,
                        cudaStream_t st);
 
+// Fused QKV projection + window attention (csrc/qkv_attention.cu), 6 heads x 32.
+struct QaArgs {
+  __half* out;        // AO rows [plane tokens][ld_out]; head h's 32 columns at h * 32
+  int ld_out;
+  const float* qb;    // [6][32] q bias (zero in the pad)
+  const float* vb;    // [6][32] v bias (zero in the pad)
+  const float* ls;    // [6] exp(min(logit_scale, ln 100)) * log2 e
+  const float* bias;  // [6][576] compact position-bias table * log2 e
+  int B;              // images in the plane
+  int nw_img;         // windows per image (window rows x nww)
+  int nww;            // windows per window row
+  int wp;             // plane width
+  int hp_l;           // plane rows (the output row index: (img * hp_l + y) * wp + x)
+  int ghp;            // global padded rows (the shift mask's plane)
+  int y_base, y_mod;  // window row wh covers plane rows (y_base + 8 wh + ty) % y_mod
+  int shift;          // 0 or window / 2 (columns roll by it; the mask needs it)
+  int wh_off;         // global window row of local window row 0 (band plans)
+  int nwin_total;     // windows of the launch (B * nw_img)
+};
+
+// mapX: make_map_nhwc over the X16 plane with 4 x 4 boxes; mapW: Wqkv [6 x 96][192]
+// (head h: rows h * 96 + q 0-31, k 32-63, v 64-95; 192-row boxes: a head pair).
+cudaError_t launch_qkv_attention(const CUtensorMap& mapX, const CUtensorMap& mapW,
+                                 const QaArgs& a, cudaStream_t st);
+// The fused kernel's compact position-bias table from the expanded one.
+cudaError_t launch_cpb_compact(const float* full, float* compact, int heads, cudaStream_t st);
+
 // TMA descriptor helpers (driver entry point resolved at first use).
 bool make_map_rows(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols_padded,
                    uint32_t box_rows);

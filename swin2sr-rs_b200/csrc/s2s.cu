@@ -2,6 +2,7 @@
 // g_s2s_err, so they are compiled together instead of with relocatable device code.
 #include "gemm_tc.cu"
 #include "attention.cu"
+#include "qkv_attention.cu"
 #include "mlp.cu"
 #include "misc.cu"
 #include "engine.cu"

@@ -78,3 +78,22 @@ def parity_report(got, want):
     clamped = float(np.abs(gc - wc).max())
     q = np.abs(np.floor(gc * 255 + 0.5) - np.floor(wc * 255 + 0.5))
     return raw, clamped, float((q > 1).mean())
+
+
+def block_launches(wt) -> int:
+    """Kernel launches per Swin block of a forward, by the library's create-time rules:
+    the fused QKV + attention kernel for 6 heads of 32 over Cp = 192 (unless two-term
+    operands or S2S_ATTN=mma), two-term operands for Cp = 64 (S2S_SPLIT overrides), the
+    fused MLP for (Cp, hidden) = (192, 384) / (64, 128) with single-term operands
+    (unless S2S_UNFUSED_MLP)."""
+    import os
+    cp = -(-wt.embed // 64) * 64
+    hid = -(-wt.embed * wt.mlp_ratio // 64) * 64
+    dp = -(-(wt.embed // wt.heads) // 16) * 16
+    sw = os.environ.get("S2S_SPLIT")
+    split = cp == 64 if sw not in ("0", "1") else sw == "1"
+    fused_attn = (not split and cp == 192 and wt.heads == 6 and dp == 32
+                  and os.environ.get("S2S_ATTN") != "mma")
+    fused_mlp = (not split and (cp, hid) in ((192, 384), (64, 128))
+                 and os.environ.get("S2S_UNFUSED_MLP", "0") in ("", "0"))
+    return (1 if fused_attn else 2) + 1 + (1 if fused_mlp else 2)

@@ -12,7 +12,7 @@ import importlib
 import numpy as np
 import pytest
 
-from s2s_testlib import adjust, oracle, pkg
+from s2s_testlib import adjust, block_launches, oracle, pkg
 
 pytestmark = pytest.mark.gpu
 
@@ -58,12 +58,13 @@ def test_stages_track_the_oracle(task):
     cmp("patch_embed", rows_to_plane(H.debug_read("S"), T, Cp, C, pl.hp, pl.wp), 2e-2)
     # block 0 (unshifted) and block 1 (shifted) of stage 0; the residual stream is
     # kept in image order, windows exist only inside the attention kernel
-    run_until(3 + 5)
+    nb = block_launches(wt)
+    run_until(3 + nb)
     cmp("layers.0.blocks.0", rows_to_plane(H.debug_read("X"), T, Cp, C, pl.hp, pl.wp), 2e-2)
-    run_until(3 + 10)
+    run_until(3 + 2 * nb)
     cmp("layers.0.blocks.1", rows_to_plane(H.debug_read("X"), T, Cp, C, pl.hp, pl.wp), 2e-2)
     # the whole first stage (blocks, conv, patch_embed, + stage input)
-    run_until(3 + 5 * depth0 + 2)
+    run_until(3 + nb * depth0 + 2)
     cmp("layers.0", rows_to_plane(H.debug_read("S"), T, Cp, C, pl.hp, pl.wp), 3e-2)
     H.debug_stop_after(-1)
     H.close()

@@ -34,10 +34,12 @@ def _launches_per_block(wt):
 def test_noalloc_attention_matches_forward(task, monkeypatch):
     import torch
 
-    # the entry point reads the single-term QKV layout: the forward it is compared
-    # with runs single-term too (S2S_SPLIT=0, read at create; the 60-wide network
-    # otherwise carries two-term operands)
+    # the entry point reads the single-term QKV layout that the QKV GEMM writes: the
+    # forward it is compared with runs single-term operands (S2S_SPLIT=0; the 60-wide
+    # network otherwise carries two-term ones) and the QKV GEMM + attention kernel pair
+    # (S2S_ATTN=mma; the 180-wide network otherwise fuses them), both read at create
     monkeypatch.setenv("S2S_SPLIT", "0")
+    monkeypatch.setenv("S2S_ATTN", "mma")
     P = pkg()
     capi = importlib.import_module("swin2sr_b200.capi")
     wt = P.weights.Weights.seeded(task, 0, True)
