@@ -83,6 +83,7 @@ def kernel_flops(wt, B, hp, wp):
         "gemm_fc1": 2 * T * C * m * C,
         "gemm_fc2": 2 * T * m * C * C,
         "mlp_fused": 2 * 2 * T * C * m * C,
+        "proj_mlp": 2 * T * C * C + 2 * 2 * T * C * m * C,
         "conv_stage": 2 * T * 9 * C * C,
         "gemm_stage_pe": 2 * T * C * C,
         "gemm_stage_pe_norm": 2 * T * C * C,
@@ -106,6 +107,7 @@ def kernel_bytes(wt, B, hp, wp):
     nq = 3 * wt.heads * dp
     return {
         "mlp_fused": T * Cp * (2 + 4 + 4 + 2),       # X16, X in; X, X16 out
+        "proj_mlp": T * Cp * (2 + 4 + 4 + 2),        # AO, X in; X, X16 out
         "gemm_proj": T * Cp * (2 + 4 + 4 + 2),       # AO, X in; X, X16 out
         "gemm_qkv": T * (Cp * 2 + nq * 2),           # X16 in; QKV out
         "window_attention": T * (nq * 2 + Cp * 2),   # QKV in; AO out
@@ -482,7 +484,8 @@ def main():
         line_k = kernel_line(name, n_launch, ms_total)
         if line_k:
             kernels[name] = line_k
-    block_kernels = ("mlp_fused", "qkv_attention", "gemm_qkv", "window_attention", "gemm_proj",
+    block_kernels = ("proj_mlp", "mlp_fused", "qkv_attention", "gemm_qkv", "window_attention",
+                     "gemm_proj",
                      "gemm_fc1", "gemm_fc2")
     roofline = None
     flops = kflops.get(dominant)

@@ -65,7 +65,7 @@ thread_local std::string g_create_error;
 // s2s_selftest creates its comparison handles with these settings of the validation
 // switches (-1: as the environment says).
 struct CreateFlags {
-  int unfused_mlp = -1, no_patch = -1, split = -1, mma_attn = -1;
+  int unfused_mlp = -1, no_patch = -1, split = -1, mma_attn = -1, unfused_proj = -1;
 };
 thread_local CreateFlags g_create_flags;
 
@@ -206,6 +206,9 @@ struct s2s_handle {
   std::map<std::string, std::pair<long, double>> prof;
   std::atomic<long long> launches{0};  // kernels launched (all calls on the handle)
   bool fused_mlp = false;      // (Cp, HIDp) has a fused MLP kernel
+  // proj + norm1 + residual run inside the fused MLP kernel (Cp = 192);
+  // S2S_UNFUSED_PROJ=1 (validation switch): the proj GEMM runs on its own
+  bool fused_proj = false;
   bool graphs = true;          // replay repeated forwards as CUDA graphs (S2S_GRAPHS=0: off)
   bool no_patch = false;       // conv_last from nine tap boxes (S2S_NO_PATCH=1: validation)
   long long stop_after = -1;   // diagnostics: launches per forward before stopping
@@ -1117,7 +1120,7 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
                                          H->heads, H->hd, H->DP, Cs, H->NQs, sp, H->NQ, lo,
                                          P->nwh_l[k], wp / 8, P->ghp, wp, sh, P->wh_off[k], st);
         });
-      {  // proj + norm1 + residual, in place
+      if (!H->fused_proj) {  // proj + norm1 + residual, in place
         Epi e = epi0();
         e.bias = bl.proj.b;
         e.ln_g = bl.n1g;
@@ -1146,15 +1149,19 @@ void forward_device(s2s_handle* H, int B, int h, int w, const float* d_in, float
         m.ln_eps = 1e-5f;
         m.x = X;
         m.x16 = X16;
-        L.run("mlp_fused", [&] {
+        m.bp = bl.proj.b;
+        m.g1 = bl.n1g;
+        m.beta1 = bl.n1b;
+        // with fused_proj the kernel starts from AO: proj + norm1 + residual, then the MLP
+        L.run(H->fused_proj ? "proj_mlp" : "mlp_fused", [&] {
           Epi eo = epi0();
           eo.o32 = X;
           eo.ld32 = Cp;
           eo.o16 = X16;
           eo.ld16 = Cs;
           const OutMaps om = out_maps(P, gemm_args(M, Cp, Cp, eo));
-          return launch_mlp(P->mX16, bl.fc1.mlp_map, bl.fc2.map, om.o32, om.o16, m, Cp, H->HIDp,
-                            st);
+          return launch_mlp(H->fused_proj ? P->mAO : P->mX16, bl.fc1.mlp_map, bl.fc2.map, om.o32,
+                            om.o16, m, Cp, H->HIDp, st, H->fused_proj ? &bl.proj.map : nullptr);
         });
       } else {
         {  // fc1 + GELU
@@ -1633,6 +1640,12 @@ int s2s_create(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors, 
     if (g && strcmp(g, "0") == 0) H->graphs = false;
     if (g_create_flags.unfused_mlp >= 0) H->fused_mlp = can_fuse && g_create_flags.unfused_mlp == 0;
     if (g_create_flags.no_patch >= 0) H->no_patch = g_create_flags.no_patch != 0;
+    H->fused_proj = H->fused_mlp && H->Cp == 192 && H->HIDp == 384;
+    const char* up = getenv("S2S_UNFUSED_PROJ");
+    if (up && strcmp(up, "1") == 0) H->fused_proj = false;
+    if (g_create_flags.unfused_proj >= 0)
+      H->fused_proj = H->fused_mlp && H->Cp == 192 && H->HIDp == 384 &&
+                      g_create_flags.unfused_proj == 0;
   }
   TensorTable T;
   for (int i = 0; i < n_tensors; i++) T.t[tensors[i].name] = &tensors[i];
@@ -1948,7 +1961,7 @@ int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors
   std::string rep;
   bool all_ok = true;
   int status = S2S_OK;
-  s2s_handle* hs[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+  s2s_handle* hs[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   auto check = [&](const char* name, double err, double tol) {
     char b[192];
     const bool ok = err <= tol;
@@ -1960,7 +1973,8 @@ int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors
   // handle k with the given validation switches; false (and the error in the report)
   // when it cannot be made
   auto make = [&](int k, int unfused_mlp, int no_patch, int split = -1,
-                  int mma_attn = -1) -> bool {
+                  int mma_attn = -1, int unfused_proj = -1) -> bool {
+    g_create_flags.unfused_proj = unfused_proj;
     g_create_flags.unfused_mlp = unfused_mlp;
     g_create_flags.no_patch = no_patch;
     g_create_flags.split = split;
@@ -2030,6 +2044,13 @@ int s2s_selftest(const s2s_config* cfg, const s2s_tensor* tensors, int n_tensors
     go = make(4, 0, 0, -1, hs[0]->fused_attn ? 1 : 0) &&
          ran(hs[4], s2s_forward(hs[4], h, w, in.data(), other.data(), nullptr), "forward");
     if (go) check("fused_vs_unfused_attention", maxabs(other.data(), eager.data(), nout), 2e-3);
+  }
+  // proj inside the fused MLP kernel against the proj GEMM on its own: the same
+  // operations in the same order
+  if (go && hs[0]->fused_proj) {
+    go = make(5, 0, 0, -1, -1, 1) &&
+         ran(hs[5], s2s_forward(hs[5], h, w, in.data(), other.data(), nullptr), "forward");
+    if (go) check("fused_vs_unfused_proj", maxabs(other.data(), eager.data(), nout), 1e-5);
   }
   for (s2s_handle*& x : hs)
     if (x) s2s_destroy(x);

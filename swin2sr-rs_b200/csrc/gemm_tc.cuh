@@ -107,15 +107,23 @@ struct MlpArgs {
   float ln_eps;
   float* x;              // [M][CP] fp32 residual stream, updated in place
   __half* x16;           // [M][CP] fp16 copy, updated in place
+  // with the proj sublayer in front (launch_mlp's mapWp given): X <- X + LN1(proj(AO) +
+  // bp), the MLP's input; then the MLP as above
+  const float* bp;       // [CP] proj bias
+  const float* g1;       // [CP] norm1 weight (zero in the pad)
+  const float* beta1;    // [CP] norm1 bias
 };
 
 // mapX: rows map of x16 (box 128 rows); mapW1: fc1 weight [HP][CP] (box 64 rows);
 // mapW2: fc2 weight [CP][HP] (box CP rows); mapX32 / mapX16o: make_map_out_rows maps of
 // x (fp32) and x16. Supported (cp, hp): (192, 384), (64, 128).
+// mapWp (optional, (cp, hp) = (192, 384)): proj weight [CP][CP] (box CP rows); mapX is
+// then the rows map of the attention output AO, and the kernel runs proj + norm1 +
+// residual first, its fp16 result staying in shared memory as fc1's operand.
 cudaError_t launch_mlp(const CUtensorMap& mapX, const CUtensorMap& mapW1,
                        const CUtensorMap& mapW2, const CUtensorMap& mapX32,
                        const CUtensorMap& mapX16o, const MlpArgs& a, int cp, int hp,
-                       cudaStream_t st);
+                       cudaStream_t st, const CUtensorMap* mapWp = nullptr);
 
 // Fused QKV projection + window attention (csrc/qkv_attention.cu), 6 heads x 32.
 struct QaArgs {

@@ -15,6 +15,16 @@
 // TMEM, warps 2..9 epilogue 1 (GELU), warps 10..17 epilogue 2 (LayerNorm +
 // residual) - the two epilogue groups work on consecutive tiles at the same time,
 // two warps per TMEM lane quarter each. All waits are bounded.
+//
+// PROJ: the attention sublayer's proj, norm1 and residual run first in the same
+// kernel (src/cpu.rs:1549-1559): the tile loaded is the attention output AO,
+//   proj         D2[tile % 2] = AO tile * Wproj^T
+//   epilogue P   x1 = X + LN1(D2 + bp): fp32 to X (TMA store, read back as epilogue
+//                2's residual), fp16 into the tile buffer in shared memory, where it
+//                is fc1's A operand
+// so the block's residual stream crosses HBM once fewer each way and the proj kernel
+// disappears. The LayerNorm group runs epilogue P of tile i before epilogue 2 of
+// tile i - 1; the two use different D2 buffers.
 #include "common.cuh"
 #include "gemm_tc.cuh"
 
@@ -32,21 +42,24 @@ struct MlpCfg {
   static constexpr int D2OFF = 2 * kMlpPart;           // D2 buffers after the two D1 buffers
   static constexpr int TUSED = D2OFF + 2 * CP;
   static constexpr uint32_t TCOLS = TUSED <= 128 ? 128 : TUSED <= 256 ? 256 : 512;
-  // a ring slot holds one fc1 part's weights (KC1 boxes of 64 x 64) or one fc2 chunk
+  // a ring slot holds one fc1 part's weights (KC1 boxes of 64 x 64), one fc2 chunk or
+  // one proj K-chunk (CP rows x 64)
   static constexpr int SLOT = KC1 * 8192 > CP * 128 ? KC1 * 8192 : CP * 128;
   // epilogue 2 per warp: two fp32 32x32 tiles (residual in / result out, 128-byte
   // swizzle) and one fp16 tile (64-byte swizzle)
   static constexpr int STG = 2 * 4096 + 2048;
   static constexpr size_t SMEM = 1024 + (size_t)KC1 * 16384 + 2 * 16384 +
                                  (size_t)STAGES * SLOT + (size_t)kMlpEpiWarps * STG +
-                                 (HP + 3 * CP) * 4 + (2 * STAGES + 12 + 2 * kMlpEpiWarps) * 8 + 16;
+                                 (HP + 6 * CP) * 4 + (2 * STAGES + 16 + 2 * kMlpEpiWarps) * 8 +
+                                 16;
 };
 
-template <int CP, int HP, int STAGES>
+template <int CP, int HP, int STAGES, bool PROJ>
 __global__ void __launch_bounds__(kMlpThreads, 1)
     k_mlp(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapW1,
           const __grid_constant__ CUtensorMap mapW2, const __grid_constant__ CUtensorMap mapX32,
-          const __grid_constant__ CUtensorMap mapX16o, const MlpArgs a) {
+          const __grid_constant__ CUtensorMap mapX16o, const __grid_constant__ CUtensorMap mapWp,
+          const MlpArgs a) {
   using Cfg = MlpCfg<CP, HP, STAGES>;
   constexpr int KC1 = Cfg::KC1, NP = Cfg::NP;
   static_assert(HP % kMlpPart == 0 && CP % 64 == 0 && NP % 2 == 0, "tile shapes");
@@ -55,21 +68,24 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sX = smem;                           // KC1 chunks: the X16 tile
+  uint8_t* sX = smem;                           // KC1 chunks: the X16 (PROJ: AO, then x1) tile
   uint8_t* sH = sX + KC1 * 16384;               // 2 hidden chunk buffers (16 KB each)
   uint8_t* ring = sH + 2 * 16384;
-  uint8_t* stgbuf = ring + STAGES * Cfg::SLOT;  // [kMlpEpiWarps][STG] epilogue-2 staging
-  float* s_vec = reinterpret_cast<float*>(stgbuf + kMlpEpiWarps * Cfg::STG);  // b1, b2, g2, beta2
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_vec + HP + 3 * CP);
+  uint8_t* stgbuf = ring + STAGES * Cfg::SLOT;  // [kMlpEpiWarps][STG] epilogue staging
+  // b1, b2, g2, beta2, bp, g1, beta1
+  float* s_vec = reinterpret_cast<float*>(stgbuf + kMlpEpiWarps * Cfg::STG);
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_vec + HP + 6 * CP);
   uint64_t* empty = full + STAGES;
   uint64_t* acc1 = empty + STAGES;   // [2] fc1 part in D1 buffer b
   uint64_t* hfull = acc1 + 2;        // [2] hidden chunk buffer b written (8 warp arrivals)
   uint64_t* acc2 = hfull + 2;        // [2] D2 buffer d complete
   uint64_t* d2free = acc2 + 2;       // [2] D2 buffer d drained (8 warp arrivals)
-  uint64_t* xfull = d2free + 2;      // X16 tile landed
-  uint64_t* xfree = xfull + 1;       // fc1 of the tile retired: X16 buffer reusable
+  uint64_t* xfull = d2free + 2;      // X16 (AO) tile landed
+  uint64_t* xfree = xfull + 1;       // fc1 of the tile retired: tile buffer reusable
   uint64_t* fin = xfree + 2;
-  uint64_t* rbar = fin + 1;          // [kMlpEpiWarps][2] residual tile landed
+  uint64_t* accp = fin + 1;          // [2] PROJ: proj result in D2 buffer d
+  uint64_t* x1ready = accp + 2;      // PROJ: x1 (fp16) in the tile buffer (8 warp arrivals)
+  uint64_t* rbar = x1ready + 1;      // [kMlpEpiWarps][2] residual tile landed
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rbar + 2 * kMlpEpiWarps);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -81,6 +97,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     tma_prefetch_desc(&mapW2);
     tma_prefetch_desc(&mapX32);
     tma_prefetch_desc(&mapX16o);
+    if (PROJ) tma_prefetch_desc(&mapWp);
     for (int s = 0; s < STAGES; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -90,10 +107,12 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       mbar_init(&hfull[b], kMlpEpiWarps);
       mbar_init(&acc2[b], 1);
       mbar_init(&d2free[b], kMlpEpiWarps);
+      mbar_init(&accp[b], 1);
     }
     mbar_init(xfull, 1);
     mbar_init(xfree, 1);
     mbar_init(fin, 1);
+    mbar_init(x1ready, kMlpEpiWarps);
     for (int k = 0; k < 2 * kMlpEpiWarps; k++) mbar_init(&rbar[k], 1);
     fence_barrier_init();
   }
@@ -106,13 +125,14 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   pdl_trigger();
-  pdl_wait();  // the previous kernel's outputs (X, X16) are complete
+  pdl_wait();  // the previous kernel's outputs (X, X16 or AO) are complete
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- producer
-      // Ring order = MMA order: W1 part 0, W1 part 1, then per part j: W2 chunk j and
-      // (j + 2 < NP) W1 part j+2. The next tile's X16 follows its xfree.
+      // Ring order = MMA order: (PROJ: Wproj chunks 0..KC1-1,) W1 part 0, W1 part 1,
+      // then per part j: W2 chunk j and (j + 2 < NP) W1 part j+2. The next tile's
+      // X16 / AO follows its xfree.
       uint32_t kit = 0;
       bool ok = true;
       auto slot_wait = [&]() -> int {
@@ -120,6 +140,14 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         if (kit >= STAGES && !mbar_wait(&empty[s], ((kit / STAGES) - 1) & 1, DEV_TIMEOUT_EMPTY))
           return -1;
         return s;
+      };
+      auto load_wp = [&](int c) -> bool {
+        const int s = slot_wait();
+        if (s < 0) return false;
+        mbar_arrive_expect_tx(&full[s], CP * 128);
+        tma_load_2d(ring + s * Cfg::SLOT, &mapWp, &full[s], c * 64, 0);
+        kit++;
+        return true;
       };
       auto load_w1 = [&](int j) -> bool {
         const int s = slot_wait();
@@ -145,7 +173,10 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       if ((int)blockIdx.x < num_tiles) load_x(blockIdx.x);
       int i = 0;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
-        ok = load_w1(0) && load_w1(1);
+        if constexpr (PROJ) {
+          for (int c = 0; c < KC1 && ok; c++) ok = load_wp(c);
+        }
+        ok = ok && load_w1(0) && load_w1(1);
         for (int j = 0; j < NP && ok; j++) {
           ok = load_w2(j);
           if (ok && j + 2 < NP) ok = load_w1(j + 2);
@@ -193,9 +224,35 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
         if (!mbar_wait(xfull, i & 1, DEV_TIMEOUT_FULL)) break;
         tc_fence_after();
-        ok = fc1(0) && fc1(1);
         const int db = i & 1;
         const uint32_t d2 = tmem + (uint32_t)(Cfg::D2OFF + db * CP);
+        if constexpr (PROJ) {
+          // D2 buffer db held tile i-2 until its epilogue 2 drained it
+          if (i >= 2 && !mbar_wait(&d2free[db], (uint32_t)(((i >> 1) - 1) & 1), DEV_TIMEOUT_ACC))
+            break;
+          tc_fence_after();
+          for (int c = 0; c < KC1 && ok; c++) {
+            const int s = slot_full();
+            if (s < 0) {
+              ok = false;
+              break;
+            }
+            const uint64_t ad = sw128_desc(smem_u32(sX + c * 16384));
+            const uint64_t bd = sw128_desc(smem_u32(ring + s * Cfg::SLOT));
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+              tc_mma_f16(d2, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), id2,
+                         (c | kk) != 0 ? 1u : 0u);
+            tc_commit(&empty[s]);
+            kit++;
+          }
+          if (!ok) break;
+          tc_commit(&accp[db]);
+          // x1 (fp16) replaced AO in the tile buffer, and D2 buffer db is drained
+          if (!mbar_wait(x1ready, i & 1, DEV_TIMEOUT_ACC)) break;
+          tc_fence_after();
+        }
+        ok = fc1(0) && fc1(1);
         for (int j = 0; j < NP && ok; j++) {
           // hidden chunk j written (and D1 buffer j % 2 drained) by epilogue 1
           if (!mbar_wait(&hfull[j & 1], (uint32_t)((i * (NP / 2) + (j >> 1)) & 1), DEV_TIMEOUT_ACC)) {
@@ -203,7 +260,8 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
             break;
           }
           // D2 buffer db held tile i-2 until its epilogue 2 drained it
-          if (j == 0 && i >= 2 && !mbar_wait(&d2free[db], (uint32_t)(((i >> 1) - 1) & 1), DEV_TIMEOUT_ACC)) {
+          if (!PROJ && j == 0 && i >= 2 &&
+              !mbar_wait(&d2free[db], (uint32_t)(((i >> 1) - 1) & 1), DEV_TIMEOUT_ACC)) {
             ok = false;
             break;
           }
@@ -242,6 +300,11 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       s_vec[HP + c] = a.b2[c];
       s_vec[HP + CP + c] = a.g2[c];
       s_vec[HP + 2 * CP + c] = a.beta2[c];
+      if (PROJ) {
+        s_vec[HP + 3 * CP + c] = a.bp[c];
+        s_vec[HP + 4 * CP + c] = a.g1[c];
+        s_vec[HP + 5 * CP + c] = a.beta1[c];
+      }
     }
     asm volatile("bar.sync 1, %0;" ::"r"(64 * kMlpEpiWarps) : "memory");
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
@@ -287,25 +350,119 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         }
       }
     } else {
-      // ---- epilogue 2: X <- X + LN2(D2 + b2), X16 <- fp16(X), through TMA
+      // ---- the LayerNorm group: epilogue P (PROJ) and epilogue 2
       uint8_t* wf32 = stgbuf + gw * Cfg::STG;
       uint8_t* f16 = wf32 + 2 * 4096;
       uint64_t* wrb = rbar + 2 * gw;
       const int sw128 = lane & 7, sw64 = (lane >> 1) & 3;  // this row's swizzle phases
       uint32_t jcnt = 0;
-      int i = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
+      // request residual chunk c of this warp's 32 rows into staging buffer jb
+      auto res_load = [&](int jb, int c, int row0) {
+        mbar_arrive_expect_tx(&wrb[jb], 4096);
+        tma_load_2d(wf32 + jb * 4096, &mapX32, &wrb[jb], c * 32, row0);
+      };
+      // ---- epilogue P: x1 = X + LN1(D2 + bp) -> X (fp32), tile buffer (fp16)
+      auto epi_p = [&](int t, int i) -> bool {
+        const int row0 = t * 128 + q * 32;
+        const int db = i & 1;
+        const uint32_t td2 = tq + (uint32_t)(Cfg::D2OFF + db * CP);
+        if (lane == 0 && half < CP / 32) {
+          bulk_wait_read<0>();
+          res_load(jcnt & 1, half, row0);
+        }
+        if (!mbar_wait(&accp[db], (uint32_t)((i >> 1) & 1), DEV_TIMEOUT_ACC)) return false;
+        tc_fence_after();
+        // row sums of x and x^2 in column order, as the GEMM LayerNorm epilogue
+        float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < CP / 32; c++) {
+          float v[32];
+          tmem_ld32(td2 + (uint32_t)(c * 32), v);
+#pragma unroll
+          for (int u = 0; u < 32; u++) {
+            const float x = v[u] + s_vec[HP + 3 * CP + c * 32 + u];
+            s1 += x;
+            s2 += x * x;
+          }
+        }
+        const float nf = (float)a.ln_n;
+        const float mean = s1 / nf;
+        const float rstd = 1.0f / sqrtf(fmaxf(s2 / nf - mean * mean, 0.0f) + a.ln_eps);
+        const float nmr = -mean * rstd;
+#pragma unroll 1
+        for (int c = half; c < CP / 32; c += 2, jcnt++) {
+          const int jb = jcnt & 1;
+          float* f32 = reinterpret_cast<float*>(wf32 + jb * 4096);
+          float v[32];
+          tmem_ld32(td2 + (uint32_t)(c * 32), v);
+          if (lane == 0) {
+            bulk_wait_read<0>();
+            if (c + 2 < CP / 32) res_load(jb ^ 1, c + 2, row0);
+          }
+          if (!mbar_wait(&wrb[jb], (jcnt >> 1) & 1, DEV_TIMEOUT_FULL)) return false;
+          const int cl0 = c * 32;
+#pragma unroll
+          for (int u = 0; u < 8; u++) {
+            const float4 bb = *reinterpret_cast<const float4*>(s_vec + HP + 3 * CP + cl0 + 4 * u);
+            const float4 gg = *reinterpret_cast<const float4*>(s_vec + HP + 4 * CP + cl0 + 4 * u);
+            const float4 be = *reinterpret_cast<const float4*>(s_vec + HP + 5 * CP + cl0 + 4 * u);
+            float4* slot = reinterpret_cast<float4*>(f32 + lane * 32 + ((u ^ sw128) << 2));
+            const float4 rr = *slot;
+            float x[4] = {v[4 * u] + bb.x, v[4 * u + 1] + bb.y, v[4 * u + 2] + bb.z,
+                          v[4 * u + 3] + bb.w};
+            x[0] = fmaf(fmaf(x[0], rstd, nmr), gg.x, be.x) + rr.x;
+            x[1] = fmaf(fmaf(x[1], rstd, nmr), gg.y, be.y) + rr.y;
+            x[2] = fmaf(fmaf(x[2], rstd, nmr), gg.z, be.z) + rr.z;
+            x[3] = fmaf(fmaf(x[3], rstd, nmr), gg.w, be.w) + rr.w;
+            *slot = make_float4(x[0], x[1], x[2], x[3]);
+            v[4 * u] = x[0];
+            v[4 * u + 1] = x[1];
+            v[4 * u + 2] = x[2];
+            v[4 * u + 3] = x[3];
+          }
+          // fp16 x1 into the tile buffer: K-chunk c / 2, 16-byte pieces (c % 2) * 4 + m
+          uint8_t* xrow = sX + (c >> 1) * 16384 + r * 128;
+#pragma unroll
+          for (int m = 0; m < 4; m++) {
+            const __half2 h0 = __floats2half2_rn(v[8 * m], v[8 * m + 1]);
+            const __half2 h1 = __floats2half2_rn(v[8 * m + 2], v[8 * m + 3]);
+            const __half2 h2 = __floats2half2_rn(v[8 * m + 4], v[8 * m + 5]);
+            const __half2 h3 = __floats2half2_rn(v[8 * m + 6], v[8 * m + 7]);
+            *reinterpret_cast<uint4*>(xrow + ((((c & 1) * 4 + m) ^ (r & 7)) << 4)) =
+                make_uint4(*reinterpret_cast<const uint32_t*>(&h0),
+                           *reinterpret_cast<const uint32_t*>(&h1),
+                           *reinterpret_cast<const uint32_t*>(&h2),
+                           *reinterpret_cast<const uint32_t*>(&h3));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&mapX32, f32, cl0, row0);
+            bulk_commit();
+          }
+        }
+        // x1 is fc1's operand now; D2 buffer db is drained
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(x1ready);
+        return true;
+      };
+      // ---- epilogue 2: X <- X + LN2(D2 + b2), X16 <- fp16(X), through TMA
+      auto epi_2 = [&](int t, int i) -> bool {
         const int row0 = t * 128 + q * 32;  // this warp's 32 rows as a TMA box origin
         const int db = i & 1;
         const uint32_t td2 = tq + (uint32_t)(Cfg::D2OFF + db * CP);
-        // the first residual tile is requested before waiting for fc2
+        // the first residual tile is requested before waiting for fc2 (with PROJ it is
+        // epilogue P's x1: its stores must have landed first)
         if (lane == 0 && half < CP / 32) {
+          if (PROJ) {
+            bulk_wait<0>();
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+          }
           bulk_wait_read<0>();
-          mbar_arrive_expect_tx(&wrb[jcnt & 1], 4096);
-          tma_load_2d(wf32 + (jcnt & 1) * 4096, &mapX32, &wrb[jcnt & 1], half * 32, row0);
+          res_load(jcnt & 1, half, row0);
         }
-        if (!mbar_wait(&acc2[db], (uint32_t)((i >> 1) & 1), DEV_TIMEOUT_ACC)) break;
+        if (!mbar_wait(&acc2[db], (uint32_t)((i >> 1) & 1), DEV_TIMEOUT_ACC)) return false;
         tc_fence_after();
         // row sums of x and x^2 in column order (the bias add two lanes at a time)
         float s1 = 0.0f, s2 = 0.0f;
@@ -349,15 +506,9 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
             // the fp16 tile and the other fp32 buffer are free once every earlier
             // store has read them; then the next chunk's residual goes there
             bulk_wait_read<0>();
-            if (c + 2 < CP / 32) {
-              mbar_arrive_expect_tx(&wrb[jb ^ 1], 4096);
-              tma_load_2d(wf32 + (jb ^ 1) * 4096, &mapX32, &wrb[jb ^ 1], (c + 2) * 32, row0);
-            }
+            if (c + 2 < CP / 32) res_load(jb ^ 1, c + 2, row0);
           }
-          if (!mbar_wait(&wrb[jb], (jcnt >> 1) & 1, DEV_TIMEOUT_FULL)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait(&wrb[jb], (jcnt >> 1) & 1, DEV_TIMEOUT_FULL)) return false;
           const int cl0 = c * 32;
 #pragma unroll
           for (int u = 0; u < 8; u++) {
@@ -400,7 +551,23 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
             bulk_commit();
           }
         }
+        return true;
+      };
+      int i = 0;
+      int tprev = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
+        if constexpr (PROJ) {
+          // epilogue P of this tile first (fc1 waits for it), then epilogue 2 of the
+          // previous one (its fc2 ran meanwhile)
+          ok = epi_p(t, i);
+          if (ok && tprev >= 0) ok = epi_2(tprev, i - 1);
+          tprev = t;
+        } else {
+          ok = epi_2(t, i);
+        }
       }
+      if (PROJ && ok && tprev >= 0) epi_2(tprev, i - 1);
       if (lane == 0) bulk_wait<0>();
     }
   }
@@ -413,31 +580,36 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   }
 }
 
-template <int CP, int HP, int STAGES>
+template <int CP, int HP, int STAGES, bool PROJ>
 cudaError_t launch_mlp_t(const CUtensorMap& mX, const CUtensorMap& mW1, const CUtensorMap& mW2,
-                         const CUtensorMap& mX32, const CUtensorMap& mX16o, const MlpArgs& a,
-                         cudaStream_t st) {
+                         const CUtensorMap& mX32, const CUtensorMap& mX16o,
+                         const CUtensorMap& mWp, const MlpArgs& a, cudaStream_t st) {
   using Cfg = MlpCfg<CP, HP, STAGES>;
   static LaunchSetup setup;
   int ctas = 0;
   const cudaError_t err =
-      resident_ctas(setup, k_mlp<CP, HP, STAGES>, kMlpThreads, Cfg::SMEM, &ctas);
+      resident_ctas(setup, k_mlp<CP, HP, STAGES, PROJ>, kMlpThreads, Cfg::SMEM, &ctas);
   if (err != cudaSuccess) return err;
   const int tiles = (a.M + 127) / 128;
   const int G = tiles < ctas ? tiles : ctas;
-  return launch_pdl(k_mlp<CP, HP, STAGES>, dim3(G), dim3(kMlpThreads), Cfg::SMEM, st, mX, mW1, mW2,
-                    mX32, mX16o, a);
+  return launch_pdl(k_mlp<CP, HP, STAGES, PROJ>, dim3(G), dim3(kMlpThreads), Cfg::SMEM, st, mX,
+                    mW1, mW2, mX32, mX16o, mWp, a);
 }
 
 }  // namespace
 
 cudaError_t launch_mlp(const CUtensorMap& mX, const CUtensorMap& mW1, const CUtensorMap& mW2,
                        const CUtensorMap& mX32, const CUtensorMap& mX16o, const MlpArgs& a, int cp,
-                       int hp, cudaStream_t st) {
+                       int hp, cudaStream_t st, const CUtensorMap* mWp) {
+  if (mWp) {
+    if (cp == 192 && hp == 384 && a.bp && a.g1 && a.beta1)
+      return launch_mlp_t<192, 384, 2, true>(mX, mW1, mW2, mX32, mX16o, *mWp, a, st);
+    return cudaErrorNotSupported;
+  }
   if (cp == 192 && hp == 384)
-    return launch_mlp_t<192, 384, 2>(mX, mW1, mW2, mX32, mX16o, a, st);
+    return launch_mlp_t<192, 384, 2, false>(mX, mW1, mW2, mX32, mX16o, mX, a, st);
   if (cp == 64 && hp == 128)
-    return launch_mlp_t<64, 128, 4>(mX, mW1, mW2, mX32, mX16o, a, st);
+    return launch_mlp_t<64, 128, 4, false>(mX, mW1, mW2, mX32, mX16o, mX, a, st);
   return cudaErrorNotSupported;
 }
 

@@ -85,7 +85,8 @@ def block_launches(wt) -> int:
     the fused QKV + attention kernel for 6 heads of 32 over Cp = 192 (unless two-term
     operands or S2S_ATTN=mma), two-term operands for Cp = 64 (S2S_SPLIT overrides), the
     fused MLP for (Cp, hidden) = (192, 384) / (64, 128) with single-term operands
-    (unless S2S_UNFUSED_MLP)."""
+    (unless S2S_UNFUSED_MLP), with proj inside it at Cp = 192 (unless
+    S2S_UNFUSED_PROJ=1)."""
     import os
     cp = -(-wt.embed // 64) * 64
     hid = -(-wt.embed * wt.mlp_ratio // 64) * 64
@@ -96,4 +97,5 @@ def block_launches(wt) -> int:
                   and os.environ.get("S2S_ATTN") != "mma")
     fused_mlp = (not split and (cp, hid) in ((192, 384), (64, 128))
                  and os.environ.get("S2S_UNFUSED_MLP", "0") in ("", "0"))
-    return (1 if fused_attn else 2) + 1 + (1 if fused_mlp else 2)
+    fused_proj = fused_mlp and cp == 192 and os.environ.get("S2S_UNFUSED_PROJ") != "1"
+    return (1 if fused_attn else 2) + (1 if fused_proj else 1 + (1 if fused_mlp else 2))

@@ -181,8 +181,7 @@ def test_bench_kernel_accounting_adds_up_to_the_forward():
     hp, wp = 248, 328
     f = bench.kernel_flops(wt, 1, hp, wp)
     blocks, stages = sum(wt.depths), len(wt.depths)
-    per_forward = {"qkv_attention": blocks, "gemm_proj": blocks,
-                   "mlp_fused": blocks, "conv_stage": stages, "gemm_stage_pe": stages,
+    per_forward = {"qkv_attention": blocks, "proj_mlp": blocks, "conv_stage": stages, "gemm_stage_pe": stages,
                    "gemm_patch_embed": 1, "conv_after_body": 1, "conv_first": 1,
                    "conv_before_upsample": 1, "conv_upsample0": 1, "conv_upsample1": 1,
                    "conv_last": 1}
@@ -192,6 +191,7 @@ def test_bench_kernel_accounting_adds_up_to_the_forward():
     assert f["mlp_fused"] == f["gemm_fc1"] + f["gemm_fc2"]
     # the fused QKV + attention kernel counts what the QKV GEMM and attention kernel do
     assert f["qkv_attention"] == f["gemm_qkv"] + f["window_attention"]
+    assert f["proj_mlp"] == f["gemm_proj"] + f["mlp_fused"]
     T, Cp = hp * wp, 192
     assert bench.kernel_bytes(wt, 1, hp, wp)["mlp_fused"] == T * Cp * 12
 

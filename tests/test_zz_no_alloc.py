@@ -8,26 +8,17 @@ one stream, so the second call rebuilds the fixed row table the first one used.
 Both results must match the forward's. The file is named to be collected last.
 """
 import importlib
-import os
 
 import numpy as np
 import pytest
 
-from s2s_testlib import adjust, pkg
+from s2s_testlib import adjust, block_launches, pkg
 
 pytestmark = pytest.mark.gpu
 
 # The same kernel on the same fp16 inputs: identical results are expected; the
 # tolerance is one fp16 step at |x| <= 1.
 TOL = 1e-3
-
-
-def _launches_per_block(wt):
-    fused = (-(-wt.embed // 64) * 64, -(-wt.embed * wt.mlp_ratio // 64) * 64) in \
-        ((192, 384), (64, 128))
-    if os.environ.get("S2S_UNFUSED_MLP", "0") not in ("", "0"):
-        fused = False
-    return 4 if fused else 5  # qkv, attention, proj, mlp (fc1 + fc2 unfused)
 
 
 @pytest.mark.parametrize("task", ["lightweight_sr", "classical_sr"])
@@ -51,7 +42,7 @@ def test_noalloc_attention_matches_forward(task, monkeypatch):
     H = capi.Handle(wt)
     try:
         want = {}
-        for block, stop in ((0, 3 + 2), (1, 3 + _launches_per_block(wt) + 2)):
+        for block, stop in ((0, 3 + 2), (1, 3 + block_launches(wt) + 2)):
             H.debug_stop_after(stop)  # pad, conv_first, patch_embed, [block 0,] qkv, attention
             H.forward_batch(x)
             qkv = H.debug_read("QKV")
