@@ -300,6 +300,33 @@ def test_unfused_mlp_path_matches_the_fused_kernel(task, monkeypatch):
     assert err <= 1e-4
 
 
+@pytest.mark.parametrize("switch", ["S2S_UNFUSED_PROJ", "S2S_ATTN"])
+def test_fused_block_kernels_match_their_plain_forms(switch, monkeypatch):
+    """The 180-wide block runs as two kernels by default: QKV + attention fused on
+    tcgen05, and proj + norm1 + residual inside the fused MLP. S2S_UNFUSED_PROJ=1 runs
+    proj as its own GEMM (the same operations in the same order: equal to fp32
+    rounding); S2S_ATTN=mma runs the QKV GEMM + mma.sync attention pair (other
+    accumulation orders: within 1e-3). Both read at create."""
+    capi = importlib.import_module("swin2sr_b200.capi")
+    P = pkg()
+    wt = P.weights.Weights.seeded("classical_sr", 0, True)
+    x = adjust(wt, np.random.default_rng(29).random((2, 3, 27, 43), dtype=np.float32))
+    H = capi.Handle(wt)
+    try:
+        fused = H.forward_batch(x)[0]
+    finally:
+        H.close()
+    monkeypatch.setenv(switch, "1" if switch == "S2S_UNFUSED_PROJ" else "mma")
+    H = capi.Handle(wt)
+    try:
+        plain = H.forward_batch(x)[0]
+    finally:
+        H.close()
+    err = float(np.abs(fused - plain).max())
+    print(f"{switch}: fused vs plain max-abs {err:.3e}")
+    assert err <= (1e-5 if switch == "S2S_UNFUSED_PROJ" else 1e-3)
+
+
 @pytest.mark.parametrize("task,h,w", [("classical_sr", 33, 41), ("classical_sr_x2", 29, 37),
                                       ("real_sr", 21, 26), ("compressed_sr", 17, 22)])
 def test_conv_last_patches_match_the_tap_boxes(task, h, w, monkeypatch):
@@ -374,6 +401,9 @@ def test_selftest_runs_every_consistency_check(task):
     rc, rep = capi.selftest(wt)
     print(rep)
     assert rc == capi.S2S_OK, rep
-    for name in ("batch_vs_single", "graph_replay_vs_eager", "patches_vs_tap_boxes",
-                 "fused_vs_unfused_mlp", "two_term_vs_single_term"):
+    names = ["batch_vs_single", "graph_replay_vs_eager", "patches_vs_tap_boxes",
+             "fused_vs_unfused_mlp", "two_term_vs_single_term"]
+    if wt.embed == 180:
+        names += ["fused_vs_unfused_attention", "fused_vs_unfused_proj"]
+    for name in names:
         assert f"{name} ok" in rep, rep
