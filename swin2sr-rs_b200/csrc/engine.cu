@@ -69,8 +69,11 @@ struct CreateFlags {
 };
 thread_local CreateFlags g_create_flags;
 
-// Whether 180-wide handles run QKV + attention as the one fused kernel by default.
-constexpr bool kFusedAttnDefault = true;
+// Whether 180-wide handles run QKV + attention as the one fused kernel by default. Not
+// today: on classical-x4 (B200) the fused kernel takes 111 us per block against 87 us
+// for the QKV GEMM + mma.sync attention pair (its per-head epilogue stages are
+// latency-bound with one CTA per SM); S2S_ATTN=fused selects it.
+constexpr bool kFusedAttnDefault = false;
 
 struct S2SError {
   int code;

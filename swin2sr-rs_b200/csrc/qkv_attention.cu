@@ -15,7 +15,8 @@
 //   QKV[j] = X Wqkv[j]^T     (N = 96: the head's q, k and v)
 //   S[j]   = Q[j] K[j]^T     (128 x 128: both windows' keys; a row reads its own 64)
 //   O[j]   = P[j] V[j]       (P rows hold zeros for the other window's keys)
-// and three epilogue warp groups, one thread per tile row:
+// and three epilogue warp groups, one thread per tile row (the softmax group two
+// warps per row set, 32 keys each):
 //   E1  q, k -> + q_bias, L2-normalised (F.normalize, eps 1e-12), q times
 //       exp(min(logit_scale, ln 100)) log2 e -> fp16 -> shared (the S operands);
 //   E2  S row (own window) + position bias (a compact 15 x 15 relative table per head,
@@ -35,7 +36,7 @@
 namespace s2s {
 namespace {
 
-constexpr int kQaThreads = 448;  // TMA, MMA, and three epilogue groups of four warps
+constexpr int kQaThreads = 576;  // TMA, MMA, E1 (4 warps), E2 (8), E3 (4)
 constexpr int kQaHeads = 6;
 constexpr int kQaGroups = 3;       // head pairs
 constexpr int kBiasStride = 40;    // compact bias table: index 40 (dy + 7) + dx + 7
@@ -48,7 +49,8 @@ constexpr int kOffP = 155648;      // P: 2 K-chunks (keys of window 0 / 1) of [1
 constexpr int kOffVt = 188416;     // V^T per head of the pair: 2 K-chunks (tokens) of [32][64]
 constexpr int kOffBias = 204800;   // [2][576] fp32
 constexpr int kOffVec = kOffBias + 2 * kBiasPerHead * 4;  // q bias, v bias [2][32], scale [2]
-constexpr int kOffBar = kOffVec + 160 * 4;
+constexpr int kOffRed = kOffVec + 160 * 4;      // E2 partial max / sum [2][2][128]
+constexpr int kOffBar = kOffRed + 512 * 4;
 constexpr int kQaBars = 30;
 constexpr size_t kQaSmem = 1024 + kOffBar + kQaBars * 8 + 16;
 static_assert(kQaSmem <= 232448, "shared memory");
@@ -62,7 +64,7 @@ __device__ __forceinline__ uint32_t h2u(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// 14 warps: an SM sub-partition holds 4 of them, so 128 registers each
+// 18 warps: an SM sub-partition holds up to 5 of them, so 96 registers each
 __global__ void __launch_bounds__(kQaThreads, 1)
     k_qkv_attention(const __grid_constant__ CUtensorMap mapX,
                     const __grid_constant__ CUtensorMap mapW, const QaArgs a) {
@@ -97,6 +99,7 @@ __global__ void __launch_bounds__(kQaThreads, 1)
   uint64_t* fin = bars + 22;       // every MMA of the CTA retired
   uint64_t* vready = bars + 23;    // [2] V^T of slot j in shared; its v TMEM drained (4)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 25);
+  float* sRed = reinterpret_cast<float*>(smem + kOffRed);  // [max|sum][half][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_tiles = (a.nwin_total + 1) / 2;
@@ -117,14 +120,14 @@ __global__ void __launch_bounds__(kQaThreads, 1)
       mbar_init(&qkv_acc[j], 1);
       mbar_init(&qkready[j], 4);
       mbar_init(&s_acc[j], 1);
-      mbar_init(&sfree[j], 4);
+      mbar_init(&sfree[j], 8);
       mbar_init(&vt_free[j], 1);
       mbar_init(&o_acc[j], 1);
       mbar_init(&o_free[j], 4);
       mbar_init(&vready[j], 4);
     }
     mbar_init(s_done, 1);
-    mbar_init(p_ready, 4);
+    mbar_init(p_ready, 8);
     mbar_init(pv_done, 1);
     mbar_init(fin, 1);
     fence_barrier_init();
@@ -295,7 +298,12 @@ __global__ void __launch_bounds__(kQaThreads, 1)
         if (did) {
           t_idle = 0;
           spins = 0;
-        } else if ((++spins & 255u) == 0) {
+        } else {
+          // back off: the epilogue warps sharing this warp's sub-partition need its
+          // issue slots more than an idle poll does
+          __nanosleep(64);
+        }
+        if (!did && (++spins & 255u) == 0) {
           const uint64_t now = global_timer_ns();
           if (t_idle == 0) {
             t_idle = now;
@@ -368,14 +376,20 @@ __global__ void __launch_bounds__(kQaThreads, 1)
         if (lane == 0) mbar_arrive(&qkready[j]);
       }
     }
-  } else if (warp < 10) {
+  } else if (warp < 14) {
     // -------------------------------------------------------------- E2: softmax
+    // two warps per TMEM lane quarter, each with 32 of the row's 64 keys; the row's
+    // max and sum combine through shared memory (named barrier 1 + q, 64 threads)
     const int q = warp & 3;
+    const int kh = (warp - 6) >> 2;        // key half
     const int r = q * 32 + lane;
     const int wsel = r >> 6, ii = r & 63;  // window of the row, its in-window token
     const int ty = tok_y(ii), tx = tok_x(ii);
-    const float* bq = sBias + kBiasStride * (ty + 7) + tx + 7;
-    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + kTmS + wsel * 64;
+    // keys kh * 32 + kk: rows 4 kh + .. of the window, so the bias base moves 160 kh
+    const float* bq = sBias + kBiasStride * (ty + 7) + tx + 7 - kBiasStride * 4 * kh;
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + kTmS + wsel * 64 + kh * 32;
+    float* redm = sRed + r;          // [half][128] at redm + 128 * half
+    float* reds = sRed + 256 + r;
     constexpr float kMask = -100.0f * 1.4426950408889634f;  // -100, in the exp2 domain
     const int nwh_g = a.ghp / 8;
     bool ok = mbar_wait(bbar, 0, DEV_TIMEOUT_FULL);
@@ -404,15 +418,15 @@ __global__ void __launch_bounds__(kQaThreads, 1)
           }
         }
       }
+      const uint32_t mb = (uint32_t)(mbits >> (32 * kh));
       for (int j = 0; j < 2; j++) {
         if (!mbar_wait(&s_acc[j], i & 1, DEV_TIMEOUT_ACC)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t sv[64];  // the row's 64 scores, then their exponentials, in place
-        tmem_ld32_nw(tq + j * 128, *reinterpret_cast<uint32_t(*)[32]>(sv));
-        tmem_ld32_nw(tq + j * 128 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        uint32_t sv[32];
+        tmem_ld32_nw(tq + j * 128, sv);
         tc_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -420,22 +434,25 @@ __global__ void __launch_bounds__(kQaThreads, 1)
         const float* bt = bq + j * kBiasPerHead;
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int k = 0; k < 64; k++) {
-          // key k of the window: bias entry (ty - ky, tx - kx), an immediate offset
+        for (int k = 0; k < 32; k++) {
           float x = __uint_as_float(sv[k]) + bt[-(kBiasStride * tok_y(k) + tok_x(k))];
-          if (masked && ((mbits >> k) & 1)) x += kMask;
+          if (masked && ((mb >> k) & 1)) x += kMask;
           sv[k] = __float_as_uint(x);
           m4[k & 3] = fmaxf(m4[k & 3], x);
         }
-        const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        redm[128 * kh] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
+        const float mx = fmaxf(redm[0], redm[128]);
         float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int k = 0; k < 64; k++) {
+        for (int k = 0; k < 32; k++) {
           const float e = ex2(__uint_as_float(sv[k]) - mx);
           sv[k] = __float_as_uint(e);
           s4[k & 3] += e;
         }
-        const float inv = 1.0f / ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+        reds[128 * kh] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
+        const float inv = 1.0f / (reds[0] + reds[128]);
         // P is free once the previous PV retired
         const int pd = 2 * i + j;
         if (pd > 0 && !mbar_wait(pv_done, (uint32_t)(pd - 1) & 1, DEV_TIMEOUT_ACC)) {
@@ -444,14 +461,14 @@ __global__ void __launch_bounds__(kQaThreads, 1)
         }
         uint8_t* prow = sP + wsel * 16384 + r * 128;
 #pragma unroll
-        for (int m = 0; m < 8; m++) {
+        for (int m = 0; m < 4; m++) {
           const float* f = reinterpret_cast<const float*>(sv + 8 * m);
           uint4 u;
           u.x = h2u(f[0] * inv, f[1] * inv);
           u.y = h2u(f[2] * inv, f[3] * inv);
           u.z = h2u(f[4] * inv, f[5] * inv);
           u.w = h2u(f[6] * inv, f[7] * inv);
-          *reinterpret_cast<uint4*>(prow + ((m ^ (r & 7)) << 4)) = u;
+          *reinterpret_cast<uint4*>(prow + (((kh * 4 + m) ^ (r & 7)) << 4)) = u;
         }
         fence_proxy_async_smem();
         __syncwarp();

@@ -82,8 +82,8 @@ def parity_report(got, want):
 
 def block_launches(wt) -> int:
     """Kernel launches per Swin block of a forward, by the library's create-time rules:
-    the fused QKV + attention kernel for 6 heads of 32 over Cp = 192 (unless two-term
-    operands or S2S_ATTN=mma), two-term operands for Cp = 64 (S2S_SPLIT overrides), the
+    the fused QKV + attention kernel for 6 heads of 32 over Cp = 192 only with
+    S2S_ATTN=fused (and single-term operands), two-term operands for Cp = 64 (S2S_SPLIT overrides), the
     fused MLP for (Cp, hidden) = (192, 384) / (64, 128) with single-term operands
     (unless S2S_UNFUSED_MLP), with proj inside it at Cp = 192 (unless
     S2S_UNFUSED_PROJ=1)."""
@@ -94,7 +94,7 @@ def block_launches(wt) -> int:
     sw = os.environ.get("S2S_SPLIT")
     split = cp == 64 if sw not in ("0", "1") else sw == "1"
     fused_attn = (not split and cp == 192 and wt.heads == 6 and dp == 32
-                  and os.environ.get("S2S_ATTN") != "mma")
+                  and os.environ.get("S2S_ATTN") == "fused")
     fused_mlp = (not split and (cp, hid) in ((192, 384), (64, 128))
                  and os.environ.get("S2S_UNFUSED_MLP", "0") in ("", "0"))
     fused_proj = fused_mlp and cp == 192 and os.environ.get("S2S_UNFUSED_PROJ") != "1"

@@ -50,14 +50,18 @@ def run_bands(wt, x, world):
             h.close()
 
 
-@pytest.mark.parametrize("task,h,w,world", [
-    ("classical_sr", 61, 45, 2),      # x4 pixelshuffle, 8 window rows
-    ("classical_sr_x2", 61, 45, 3),   # x2 pixelshuffle
-    ("lightweight_sr", 40, 30, 4),    # pixelshuffledirect
-    ("real_sr", 37, 21, 2),           # nearest+conv x4
-    ("classical_sr", 16, 30, 3),      # one window row per band; the last band is all padding
+@pytest.mark.parametrize("task,h,w,world,attn", [
+    ("classical_sr", 61, 45, 2, None),      # x4 pixelshuffle, 8 window rows
+    ("classical_sr_x2", 61, 45, 3, None),   # x2 pixelshuffle
+    ("lightweight_sr", 40, 30, 4, None),    # pixelshuffledirect
+    ("real_sr", 37, 21, 2, None),           # nearest+conv x4
+    ("classical_sr", 16, 30, 3, None),      # one window row per band; the last band is all padding
+    ("classical_sr", 61, 45, 3, "fused"),   # the fused QKV + attention kernel on bands
+    ("real_sr", 37, 21, 2, "fused"),
 ])
-def test_bands_equal_the_whole_image_forward(task, h, w, world):
+def test_bands_equal_the_whole_image_forward(task, h, w, world, attn, monkeypatch):
+    if attn:
+        monkeypatch.setenv("S2S_ATTN", attn)
     C = capi()
     P = pkg()
     wt = P.weights.Weights.seeded(task, 0, True)

@@ -300,31 +300,54 @@ def test_unfused_mlp_path_matches_the_fused_kernel(task, monkeypatch):
     assert err <= 1e-4
 
 
-@pytest.mark.parametrize("switch", ["S2S_UNFUSED_PROJ", "S2S_ATTN"])
-def test_fused_block_kernels_match_their_plain_forms(switch, monkeypatch):
-    """The 180-wide block runs as two kernels by default: QKV + attention fused on
-    tcgen05, and proj + norm1 + residual inside the fused MLP. S2S_UNFUSED_PROJ=1 runs
-    proj as its own GEMM (the same operations in the same order: equal to fp32
-    rounding); S2S_ATTN=mma runs the QKV GEMM + mma.sync attention pair (other
-    accumulation orders: within 1e-3). Both read at create."""
+@pytest.mark.parametrize("switch,value", [("S2S_UNFUSED_PROJ", "1"), ("S2S_ATTN", "fused")])
+def test_block_kernel_forms_agree(switch, value, monkeypatch):
+    """The 180-wide block runs proj + norm1 + residual inside the fused MLP kernel;
+    S2S_UNFUSED_PROJ=1 runs proj as its own GEMM (the same operations in the same
+    order: equal to fp32 rounding). S2S_ATTN=fused runs QKV + attention as one tcgen05
+    kernel instead of the QKV GEMM + mma.sync attention pair (other accumulation
+    orders: within 1e-3). Both read at create."""
     capi = importlib.import_module("swin2sr_b200.capi")
     P = pkg()
     wt = P.weights.Weights.seeded("classical_sr", 0, True)
     x = adjust(wt, np.random.default_rng(29).random((2, 3, 27, 43), dtype=np.float32))
     H = capi.Handle(wt)
     try:
-        fused = H.forward_batch(x)[0]
+        base = H.forward_batch(x)[0]
     finally:
         H.close()
-    monkeypatch.setenv(switch, "1" if switch == "S2S_UNFUSED_PROJ" else "mma")
+    monkeypatch.setenv(switch, value)
     H = capi.Handle(wt)
     try:
-        plain = H.forward_batch(x)[0]
+        other = H.forward_batch(x)[0]
     finally:
         H.close()
-    err = float(np.abs(fused - plain).max())
-    print(f"{switch}: fused vs plain max-abs {err:.3e}")
+    err = float(np.abs(base - other).max())
+    print(f"{switch}={value}: max-abs {err:.3e}")
     assert err <= (1e-5 if switch == "S2S_UNFUSED_PROJ" else 1e-3)
+
+
+@pytest.mark.parametrize("task,B,h,w", [("classical_sr", 1, 40, 56), ("classical_sr", 2, 17, 23),
+                                        ("real_sr", 1, 24, 40), ("compressed_sr", 3, 16, 16)])
+def test_fused_attention_kernel_matches_oracle(task, B, h, w, monkeypatch):
+    """S2S_ATTN=fused: the tcgen05 QKV + attention kernel (windows as TMA boxes, shift
+    mask, a missing second window of an odd window count, batches) against the oracle."""
+    monkeypatch.setenv("S2S_ATTN", "fused")
+    capi = importlib.import_module("swin2sr_b200.capi")
+    P = pkg()
+    wt = P.weights.Weights.seeded(task, 0, True)
+    x = adjust(wt, np.random.default_rng(h * 100 + w).random((B, 3, h, w), dtype=np.float32))
+    H = capi.Handle(wt)
+    try:
+        out, aux = H.forward_batch(x)
+    finally:
+        H.close()
+    O = oracle()
+    for b in range(B):
+        ref, raux = O.forward(wt, h, w, x[b])
+        check(out[b], ref, f"{task} fused attention {h}x{w} [{b}]")
+        if raux is not None:
+            check(aux[b], raux, f"{task} fused attention aux [{b}]")
 
 
 @pytest.mark.parametrize("task,h,w", [("classical_sr", 33, 41), ("classical_sr_x2", 29, 37),
