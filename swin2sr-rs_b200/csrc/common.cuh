@@ -97,7 +97,7 @@ cudaError_t resident_ctas(LaunchSetup& ls, Kern kernel, int threads, size_t smem
 
 // Error codes recorded on the device (first error wins).
 enum : unsigned { DEV_OK = 0, DEV_TIMEOUT_FULL = 1, DEV_TIMEOUT_EMPTY = 2, DEV_TIMEOUT_ACC = 3,
-                  DEV_BAD_SHAPE = 4 };
+                  DEV_BAD_SHAPE = 4, DEV_TIMEOUT_HALO = 5 };
 
 // Defined once: the library is a single translation unit (s2s.cu).
 __device__ unsigned int g_s2s_err = 0;
@@ -199,6 +199,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
       "r"(c3)
       : "memory");
+}
+
+// Warm L2 with one box of a 2-D tensor map (no shared-memory destination, no barrier;
+// boxes beyond the tensor's bounds fetch nothing).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
 }
 
 // Bulk tensor stores (shared -> global) tracked by per-thread bulk async-groups.

@@ -158,6 +158,11 @@ struct Plan {
   bool hbp[3][3] = {{false}};             // ... when the plane's conv box allows them
   // Output / residual TMA maps, built on first use for each (buffer, geometry).
   std::map<std::array<int64_t, 8>, CUtensorMap> omaps;
+  // Peer-store halo transport (band plans over NCCL unless S2S_HALO=nccl): this
+  // rank's mailbox and its neighbours' planes and mailboxes, mapped through CUDA IPC.
+  HaloMailbox* mb = nullptr;
+  HaloPeer prevp, nextp;
+  std::vector<void*> ipc_maps;
 };
 
 struct ProfEntry {
@@ -219,6 +224,7 @@ struct s2s_handle {
   // Row-band sharding (s2s_band_init / s2s_band_init_local): this handle's rank.
   int band_rank = 0, band_world = 1;
   void* nccl_comm = nullptr;                  // ncclComm_t
+  bool halo_ipc = true;                       // peer stores (S2S_HALO=nccl: NCCL send/recv)
   cudaStream_t side = nullptr;                // halo transfers overlapping the QKV GEMM
   cudaEvent_t fork = nullptr, join = nullptr;
   std::shared_ptr<s2s::LocalGroup> group;     // in-process group instead of NCCL
@@ -585,8 +591,68 @@ void* dalloc(Plan& P, size_t bytes) {
 void free_plan(Plan& P) {
   if (P.gexec) cudaGraphExecDestroy(P.gexec);
   P.gexec = nullptr;
+  for (void* p : P.ipc_maps) cudaIpcCloseMemHandle(p);
+  P.ipc_maps.clear();
+  P.mb = nullptr;
+  P.prevp = HaloPeer();
+  P.nextp = HaloPeer();
   for (void* p : P.allocs) cudaFree(p);
   P.allocs.clear();
+}
+
+// The peer-store halo transport of a band plan: export this rank's X16 and AO planes
+// and a zeroed mailbox as CUDA IPC handles, trade them with both neighbours over the
+// NCCL communicator (every rank builds its plan for the same image at the same
+// time), and map the neighbours'. Collective over the ranks, like the exchanges.
+struct IpcCard {
+  cudaIpcMemHandle_t x16, ao, mb;
+  int halo, own_rows, pad[2];
+};
+
+void setup_ipc(s2s_handle* H, Plan& P) {
+  P.mb = (HaloMailbox*)dalloc(P, sizeof(HaloMailbox));
+  IpcCard mine;
+  memset(&mine, 0, sizeof mine);
+  ck(cudaIpcGetMemHandle(&mine.x16, P.X16), "IPC handle of the X16 plane");
+  ck(cudaIpcGetMemHandle(&mine.ao, P.AO), "IPC handle of the AO plane");
+  ck(cudaIpcGetMemHandle(&mine.mb, P.mb), "IPC handle of the halo mailbox");
+  mine.halo = P.halo;
+  mine.own_rows = P.own_rows;
+  const NcclApi& api = nccl_api();
+  ncclComm_t comm = (ncclComm_t)H->nccl_comm;
+  const int prev = (P.rank + P.world - 1) % P.world, next = (P.rank + 1) % P.world;
+  IpcCard cards[2];  // from prev, from next
+  char* d = (char*)dalloc(P, 3 * sizeof(IpcCard));
+  ck(cudaMemcpy(d, &mine, sizeof mine, cudaMemcpyHostToDevice), "IPC card");
+  auto nck = [&](ncclResult_t r) {
+    if (r != ncclSuccess) fail(S2S_ERR_NCCL, std::string("IPC card exchange: ") + api.GetErrorString(r));
+  };
+  // sends to next before prev, receives from prev before next (pairs up at 2 ranks)
+  nck(api.GroupStart());
+  nck(api.Send(d, sizeof(IpcCard), ncclInt8, next, comm, H->stream));
+  nck(api.Send(d, sizeof(IpcCard), ncclInt8, prev, comm, H->stream));
+  nck(api.Recv(d + sizeof(IpcCard), sizeof(IpcCard), ncclInt8, prev, comm, H->stream));
+  nck(api.Recv(d + 2 * sizeof(IpcCard), sizeof(IpcCard), ncclInt8, next, comm, H->stream));
+  nck(api.GroupEnd());
+  ck(cudaStreamSynchronize(H->stream), "IPC card exchange");
+  ck(cudaMemcpy(cards, d + sizeof(IpcCard), sizeof cards, cudaMemcpyDeviceToHost), "IPC card");
+  auto open = [&](const cudaIpcMemHandle_t& h) {
+    void* p = nullptr;
+    ck(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "IPC mapping of a neighbour");
+    P.ipc_maps.push_back(p);
+    return p;
+  };
+  auto peer = [&](const IpcCard& c) {
+    HaloPeer q;
+    q.x16 = open(c.x16);
+    q.ao = open(c.ao);
+    q.mb = (HaloMailbox*)open(c.mb);
+    q.halo = c.halo;
+    q.own_rows = c.own_rows;
+    return q;
+  };
+  P.prevp = peer(cards[0]);
+  P.nextp = prev == next ? P.prevp : peer(cards[1]);
 }
 
 // Pixel index (within image) read by window-major token r for shift s.
@@ -779,6 +845,14 @@ Plan* get_plan(s2s_handle* H, int B, int h, int w) {
     free_plan(*P);
     fail(S2S_ERR_CUDA, "cuTensorMapEncodeTiled failed for an activation operand");
   }
+  if (band && H->nccl_comm && H->halo_ipc) {
+    try {
+      setup_ipc(H, *P);
+    } catch (...) {
+      free_plan(*P);
+      throw;
+    }
+  }
   H->plan = std::move(P);
   return H->plan.get();
 }
@@ -933,6 +1007,22 @@ void halo_exchange(s2s_handle* H, Plan* P, __half* buf, int ld, int n, bool cycl
   const size_t row = (size_t)P->wp * ld;  // halves per plane row
   HaloOp ops[4];
   const int k = halo_ops(P->rank, P->world, P->halo, P->own_rows, n, cyclic, ops);
+  if (P->mb) {
+    // peer stores: the neighbours' copy of this plane
+    auto peer_plane = [&](const HaloPeer& q) -> void* {
+      if (buf == P->X16) return q.x16;
+      if (buf == P->AO) return q.ao;
+      fail(S2S_ERR_INVALID, "halo exchange: a plane without a peer mapping");
+      return nullptr;
+    };
+    const bool has_prev = cyclic || P->rank != 0, has_next = cyclic || P->rank != P->world - 1;
+    ck(launch_halo_push(buf, has_prev ? peer_plane(P->prevp) : nullptr,
+                        has_next ? peer_plane(P->nextp) : nullptr, P->mb, &P->prevp, &P->nextp,
+                        row * 2, n, P->halo, P->own_rows, zero_edges, zero_edges, st),
+       "halo push");
+    H->launches++;
+    return;
+  }
   if (H->nccl_comm) {
     const NcclApi& api = nccl_api();
     ncclComm_t comm = (ncclComm_t)H->nccl_comm;
@@ -1847,6 +1937,11 @@ int s2s_band_init(s2s_handle* H, int rank, int world, const void* id, int id_byt
     ck(cudaStreamSynchronize(H->stream), "band init");
     release_band(H);
     if (world > 1) {
+      // halo transport: peer stores through IPC mappings, or NCCL send/recv
+      const char* ht = getenv("S2S_HALO");
+      if (ht && strcmp(ht, "nccl") != 0 && strcmp(ht, "ipc") != 0)
+        fail(S2S_ERR_INVALID, std::string("S2S_HALO must be ipc or nccl, not ") + ht);
+      H->halo_ipc = !(ht && strcmp(ht, "nccl") == 0);
       if (!id || id_bytes != (int)sizeof(ncclUniqueId))
         fail(S2S_ERR_INVALID, "s2s_band_init: the id must be the S2S_BAND_ID_BYTES of "
                               "s2s_band_unique_id");

@@ -4,10 +4,15 @@
 // shifted block a rank needs the 4 rows either side of its band (cyclically: the
 // first and last bands are neighbours through the roll's wrap), before a 3x3
 // convolution 1 row (zeros beyond the plane's true edges), before the upsampling
-// head 4 rows. Two transports move them:
-//   * NCCL point-to-point (ranks are processes, one GPU each). libnccl.so.2 is
-//     resolved at run time - the copy the process already loaded (PyTorch's) when
-//     there is one - so libs2s.so has no link-time dependency on it;
+// head 4 rows. Three transports move them:
+//   * peer stores (ranks are processes, one GPU each; the default): each rank maps
+//     its neighbours' planes and mailboxes through CUDA IPC and one kernel per
+//     exchange writes its boundary rows straight into their halo rows over NVLink,
+//     with flags in the mailboxes ordering the writes (k_halo_push);
+//   * NCCL point-to-point (S2S_HALO=nccl). libnccl.so.2 is resolved at run time -
+//     the copy the process already loaded (PyTorch's) when there is one - so
+//     libs2s.so has no link-time dependency on it. NCCL also carries the IPC
+//     handles to the neighbours when a band plan is built;
 //   * an in-process group of handles, one host thread each (tests on one GPU, and
 //     embedders that drive several GPUs from one process): device-to-device copies
 //     ordered by CUDA events, with a host barrier on either side.
@@ -54,6 +59,34 @@ inline void band_partition(int window_rows, int world, int rank, int* w0, int* w
   *w0 = rank * base + (rank < extra ? rank : extra);
   *w1 = *w0 + base + (rank < extra ? 1 : 0);
 }
+
+// ------------------------------------------------------------------ peer-store mailboxes
+// Blocks of k_halo_push (each signals its share of the rows by its own flag).
+constexpr int kHaloBlocks = 32;
+
+// One per rank and band plan, in the rank's device memory, mapped by both
+// neighbours. Words are exchange epochs (1, 2, ... per plan, the same on every rank:
+// all ranks run the same exchanges in the same order) written by the neighbours:
+//   may_push_next  my next band's top halo rows are free for exchange e (its readers
+//                  of exchange e - 1 have finished)
+//   may_push_prev  my previous band's bottom halo rows are free
+//   top_in[b]      block b of my previous band has written its share of my top halo
+//   bottom_in[b]   block b of my next band has written its share of my bottom halo
+// and two local words: seq, the last exchange this rank completed, and arrive, the
+// blocks of the running exchange that have finished.
+struct HaloMailbox {
+  unsigned may_push_next, may_push_prev;
+  unsigned top_in[kHaloBlocks], bottom_in[kHaloBlocks];
+  unsigned seq, arrive;
+};
+
+// What a rank needs of a neighbour's band plan: its planes, mailbox and layout.
+struct HaloPeer {
+  void* x16 = nullptr;
+  void* ao = nullptr;
+  HaloMailbox* mb = nullptr;
+  int halo = 0, own_rows = 0;
+};
 
 // ------------------------------------------------------------------ NCCL, resolved at run time
 struct NcclApi {

@@ -5,6 +5,7 @@
 #include "qkv_attention.cu"
 #include "mlp.cu"
 #include "misc.cu"
+#include "halo_push.cu"
 #include "engine.cu"
 #include "image.cu"
 #include "noalloc.cu"

@@ -1,8 +1,10 @@
-"""Row-band sharded forward over NCCL, one process per GPU (skipped below 2 GPUs).
+"""Row-band sharded forward across processes, one per GPU (skipped below 2 GPUs).
 
 Each rank is a spawned process on its own GPU; the communicator id comes from
-s2s_band_unique_id in the parent. The concatenated bands must equal the
-whole-image forward on one GPU exactly (the arithmetic per row is identical).
+s2s_band_unique_id in the parent. Both halo transports run: peer stores into the
+neighbours' IPC-mapped planes (the default) and NCCL send/recv (S2S_HALO=nccl).
+The concatenated bands must equal the whole-image forward on one GPU exactly (the
+arithmetic per row is identical).
 """
 import numpy as np
 import pytest
@@ -17,10 +19,11 @@ def _ngpus():
     return torch.cuda.device_count() if torch.cuda.is_available() else 0
 
 
-def _rank(rank, world, uid, task, h, w, q):
+def _rank(rank, world, uid, task, h, w, transport, q):
     import importlib
     import os
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["S2S_HALO"] = transport
     try:
         import torch
         torch.cuda.set_device(rank)
@@ -40,8 +43,9 @@ def _rank(rank, world, uid, task, h, w, q):
         q.put((rank, None, None, False, repr(e)))
 
 
+@pytest.mark.parametrize("transport", ["ipc", "nccl"])
 @pytest.mark.parametrize("task,h,w", [("classical_sr", 70, 52), ("real_sr", 45, 33)])
-def test_nccl_bands_equal_the_whole_image_forward(task, h, w):
+def test_bands_equal_the_whole_image_forward(task, h, w, transport):
     world = min(_ngpus(), 4)
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -53,7 +57,7 @@ def test_nccl_bands_equal_the_whole_image_forward(task, h, w):
     uid = C.band_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, uid, task, h, w, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, uid, task, h, w, transport, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -73,5 +77,5 @@ def test_nccl_bands_equal_the_whole_image_forward(task, h, w):
         H.close()
     got = np.concatenate([res[r][1] for r in range(world)], axis=1)
     err = float(np.abs(got - whole).max())
-    print(f"{task} {h}x{w} NCCL world {world}: bands vs whole max-abs {err:.3e}")
+    print(f"{task} {h}x{w} {transport} world {world}: bands vs whole max-abs {err:.3e}")
     assert err == 0.0
