@@ -8,8 +8,9 @@ A step is one whole-image forward of the workload (default classical-x4: one
 240x320 image -> 960x1280, seeded weights and input, see workloads.py). Multi-GPU
 (torchrun, one process per GPU), by --mode:
   band      (default for single-image workloads) the image is split into
-            window-aligned row bands, one per rank, with NCCL halo exchange
-            (s2s_forward_band); total work fixed ("scaling": "strong");
+            window-aligned row bands, one per rank, with halo exchange by peer
+            stores into the neighbours' IPC-mapped planes (S2S_HALO=nccl: NCCL
+            send/recv) (s2s_forward_band); total work fixed ("scaling": "strong");
   batch     (default for batched workloads) the batch is split across ranks with
             no communication; total work fixed;
   replicas  every rank runs its own copy of the workload (weak scaling).
@@ -552,7 +553,9 @@ def main():
                        "output": f"{h * s}x{w * s}", "padded_plane": f"{hp}x{wp}",
                        "weights": "seeded random init (seed 0)",
                        "parallelism": {"single": "single", "replicas": f"replicas x{world}",
-                                       "band": f"row bands x{world} (NCCL halos)",
+                                       "band": f"row bands x{world} ("
+                                               + ("NCCL" if os.environ.get("S2S_HALO") == "nccl"
+                                                  else "peer-store") + " halos)",
                                        "batch": f"batch split x{world}"}[mode],
                        "l2": "flushed between steps (256 MB write, outside the events)",
                        "precision": "fp16 operands, fp32 accumulate/residual/norms"},

@@ -135,20 +135,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   pdl_trigger();
-  pdl_wait();  // the previous kernel's outputs (this kernel's A operand) are complete
-
   // When all of this CTA's B (its N tile over the whole K) fits the ring's B slots -
   // a GEMM with K <= 64 * STAGES - it is loaded once and stays resident; the ring then
-  // streams A only.
+  // streams A only. B is a weight, never the previous kernel's output: its load is
+  // issued before the dependency wait and overlaps the previous kernel's tail.
   const bool bres = !a.conv && num_k <= STAGES;  // AR > 0 launches guarantee it
+  if (warp == 0 && lane == 0 && bres) {
+    mbar_arrive_expect_tx(bfull, (uint32_t)(num_k * B_BYTES));
+    for (int k = 0; k < num_k; k++) tma_load_2d(sB + k * B_BYTES, &mapB, bfull, k * 64, n0);
+  }
+  pdl_wait();  // the previous kernel's outputs (this kernel's A operand) are complete
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- producer
-      if (bres) {
-        mbar_arrive_expect_tx(bfull, (uint32_t)(num_k * B_BYTES));
-        for (int k = 0; k < num_k; k++) tma_load_2d(sB + k * B_BYTES, &mapB, bfull, k * 64, n0);
-      }
       uint32_t kit = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += G) {

@@ -24,11 +24,7 @@
 //                is fc1's A operand
 // so the block's residual stream crosses HBM once fewer each way and the proj kernel
 // disappears. The LayerNorm group runs epilogue P of tile i before epilogue 2 of
-// tile i - 1; the two use different D2 buffers. The next tile's AO lands as soon as
-// this tile's last fc1 has retired, and its proj is issued before this tile's last two
-// fc2 chunks, so epilogue P of tile i + 1 starts while the tail of tile i's hidden
-// chain still runs. The producer warms L2 with each tile's residual rows when it
-// requests the tile's AO.
+// tile i - 1; the two use different D2 buffers.
 #include "common.cuh"
 #include "gemm_tc.cuh"
 
@@ -67,7 +63,6 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   using Cfg = MlpCfg<CP, HP, STAGES>;
   constexpr int KC1 = Cfg::KC1, NP = Cfg::NP;
   static_assert(HP % kMlpPart == 0 && CP % 64 == 0 && NP % 2 == 0, "tile shapes");
-  static_assert(!PROJ || NP >= 4, "the next tile's proj is issued after fc1 of the last part");
   static_assert(Cfg::TUSED <= 512, "TMEM columns");
   static_assert(Cfg::SMEM <= 232448, "shared memory");
   extern __shared__ uint8_t smem_raw[];
@@ -135,10 +130,9 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------------------------------------------------------- producer
-      // Ring order = MMA order: W1 part 0, W1 part 1, then per part j: W2 chunk j and
-      // (j + 2 < NP) W1 part j+2. The next tile's X16 follows its xfree. PROJ: the
-      // first tile's Wproj chunks 0..KC1-1 come first; the next tile's AO and Wproj
-      // chunks follow W1 part NP-1 (after its xfree), ahead of W2 chunks NP-2, NP-1.
+      // Ring order = MMA order: (PROJ: Wproj chunks 0..KC1-1,) W1 part 0, W1 part 1,
+      // then per part j: W2 chunk j and (j + 2 < NP) W1 part j+2. The next tile's
+      // X16 / AO follows its xfree.
       uint32_t kit = 0;
       bool ok = true;
       auto slot_wait = [&]() -> int {
@@ -175,39 +169,20 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
       auto load_x = [&](int t) {
         mbar_arrive_expect_tx(xfull, KC1 * 16384);
         for (int k = 0; k < KC1; k++) tma_load_2d(sX + k * 16384, &mapX, xfull, k * 64, t * 128);
-        if constexpr (PROJ) {
-          // epilogue P's residual rows (never read before) into L2 meanwhile
-          for (int r = 0; r < 128; r += 32)
-            for (int c = 0; c < CP; c += 32) tma_prefetch_l2_2d(&mapX32, c, t * 128 + r);
-        }
       };
-      if ((int)blockIdx.x < num_tiles) {
-        load_x(blockIdx.x);
+      if ((int)blockIdx.x < num_tiles) load_x(blockIdx.x);
+      int i = 0;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
         if constexpr (PROJ) {
           for (int c = 0; c < KC1 && ok; c++) ok = load_wp(c);
         }
-      }
-      int i = 0;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
-        const bool more = t + (int)gridDim.x < num_tiles;
-        ok = load_w1(0) && load_w1(1);
+        ok = ok && load_w1(0) && load_w1(1);
         for (int j = 0; j < NP && ok; j++) {
           ok = load_w2(j);
           if (ok && j + 2 < NP) ok = load_w1(j + 2);
-          if (PROJ && ok && more && j + 3 == NP) {
-            // the next tile's AO and Wproj chunks enter right after this tile's last
-            // fc1 weights, so its proj runs before this tile's last two fc2 (whose
-            // epilogue 2 waits behind the next tile's epilogue P anyway)
-            if (!mbar_wait(xfree, i & 1, DEV_TIMEOUT_EMPTY)) {
-              ok = false;
-              break;
-            }
-            load_x(t + gridDim.x);
-            for (int c = 0; c < KC1 && ok; c++) ok = load_wp(c);
-          }
         }
         if (!ok) break;
-        if (!PROJ && more) {
+        if (t + (int)gridDim.x < num_tiles) {
           if (!mbar_wait(xfree, i & 1, DEV_TIMEOUT_EMPTY)) break;
           load_x(t + gridDim.x);
         }
@@ -246,42 +221,37 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         kit++;
         return true;
       };
-      // proj of the tile with local index ii: AO (tile buffer) x Wproj -> D2 buffer ii % 2
-      auto proj = [&](int ii) -> bool {
-        if (!mbar_wait(xfull, ii & 1, DEV_TIMEOUT_FULL)) return false;
-        const int pb = ii & 1;
-        // D2 buffer pb held tile ii-2 until its epilogue 2 drained it
-        if (ii >= 2 && !mbar_wait(&d2free[pb], (uint32_t)(((ii >> 1) - 1) & 1), DEV_TIMEOUT_ACC))
-          return false;
-        tc_fence_after();
-        const uint32_t dp = tmem + (uint32_t)(Cfg::D2OFF + pb * CP);
-        for (int c = 0; c < KC1; c++) {
-          const int s = slot_full();
-          if (s < 0) return false;
-          const uint64_t ad = sw128_desc(smem_u32(sX + c * 16384));
-          const uint64_t bd = sw128_desc(smem_u32(ring + s * Cfg::SLOT));
-#pragma unroll
-          for (int kk = 0; kk < 4; kk++)
-            tc_mma_f16(dp, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), id2,
-                       (c | kk) != 0 ? 1u : 0u);
-          tc_commit(&empty[s]);
-          kit++;
-        }
-        tc_commit(&accp[pb]);
-        return true;
-      };
-      if (PROJ && (int)blockIdx.x < num_tiles) ok = proj(0);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
+        if (!mbar_wait(xfull, i & 1, DEV_TIMEOUT_FULL)) break;
+        tc_fence_after();
         const int db = i & 1;
         const uint32_t d2 = tmem + (uint32_t)(Cfg::D2OFF + db * CP);
         if constexpr (PROJ) {
+          // D2 buffer db held tile i-2 until its epilogue 2 drained it
+          if (i >= 2 && !mbar_wait(&d2free[db], (uint32_t)(((i >> 1) - 1) & 1), DEV_TIMEOUT_ACC))
+            break;
+          tc_fence_after();
+          for (int c = 0; c < KC1 && ok; c++) {
+            const int s = slot_full();
+            if (s < 0) {
+              ok = false;
+              break;
+            }
+            const uint64_t ad = sw128_desc(smem_u32(sX + c * 16384));
+            const uint64_t bd = sw128_desc(smem_u32(ring + s * Cfg::SLOT));
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+              tc_mma_f16(d2, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), id2,
+                         (c | kk) != 0 ? 1u : 0u);
+            tc_commit(&empty[s]);
+            kit++;
+          }
+          if (!ok) break;
+          tc_commit(&accp[db]);
           // x1 (fp16) replaced AO in the tile buffer, and D2 buffer db is drained
           if (!mbar_wait(x1ready, i & 1, DEV_TIMEOUT_ACC)) break;
-        } else {
-          if (!mbar_wait(xfull, i & 1, DEV_TIMEOUT_FULL)) break;
+          tc_fence_after();
         }
-        tc_fence_after();
-        const bool more = t + (int)gridDim.x < num_tiles;
         ok = fc1(0) && fc1(1);
         for (int j = 0; j < NP && ok; j++) {
           // hidden chunk j written (and D1 buffer j % 2 drained) by epilogue 1
@@ -310,9 +280,6 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
           tc_commit(&empty[s]);
           kit++;
           if (j + 2 < NP) ok = fc1(j + 2);
-          // the next tile's proj, in the producer's ring order (its AO lands once the
-          // last fc1 above has retired)
-          if (PROJ && ok && more && j + 3 == NP) ok = proj(i + 1);
         }
         if (!ok) break;
         tc_commit(&acc2[db]);
@@ -486,11 +453,10 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         const int db = i & 1;
         const uint32_t td2 = tq + (uint32_t)(Cfg::D2OFF + db * CP);
         // the first residual tile is requested before waiting for fc2 (with PROJ it is
-        // epilogue P's x1: its stores must have landed first; only the CP / 64 store
-        // groups of the epilogue P just run, the next tile's, may still be in flight)
+        // epilogue P's x1: its stores must have landed first)
         if (lane == 0 && half < CP / 32) {
           if (PROJ) {
-            bulk_wait<CP / 64>();
+            bulk_wait<0>();
             asm volatile("fence.proxy.async.global;" ::: "memory");
           }
           bulk_wait_read<0>();
