@@ -31,7 +31,7 @@ namespace s2s {
 
 namespace {
 
-constexpr int kThreads = 320;  // producer, MMA, 8 epilogue warps
+// producer warp, MMA warp and kEpiWarps epilogue warps (a launch may take 12)
 constexpr int kEpiWarps = 8;
 constexpr int kStageFloats = 32 * 36;  // STORE_SHUFFLE2 staging: 32 rows x 32 cols, 16-B rows
 // Per epilogue warp: two fp32 32x32 tiles (residual in, result out; 128-byte swizzle)
@@ -46,8 +46,8 @@ struct TmemCols {
 };
 
 template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE, int AR = 0,
-          int WB = kWarpBuf, bool PATCH = false>
-__global__ void __launch_bounds__(kThreads, 1)
+          int WB = kWarpBuf, bool PATCH = false, int EW = kEpiWarps>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
            const __grid_constant__ OutMaps om, const GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -71,17 +71,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 "plane store (registers to global)");
   uint8_t* sA = smem;
   uint8_t* sB = smem + NA * A_SLOT;
-  uint8_t* obuf = sB + STAGES * B_SLOT;                     // [kEpiWarps][WB], 1 KB aligned
-  float* s_vec = reinterpret_cast<float*>(obuf + kEpiWarps * WB);  // bias, gamma, beta [3][BN]
+  uint8_t* obuf = sB + STAGES * B_SLOT;                     // [EW][WB], 1 KB aligned
+  float* s_vec = reinterpret_cast<float*>(obuf + EW * WB);  // bias, gamma, beta [3][BN]
   int* s_rows = reinterpret_cast<int*>(s_vec + 3 * BN);     // shuffle store: per warp, per row
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_rows + kEpiWarps * 32 * 4);
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_rows + EW * 32 * 4);
   uint64_t* empty = full + NA;
   uint64_t* accf = empty + NA;       // [2] accumulator ready
   uint64_t* acce = accf + 2;         // [2] accumulator drained
   uint64_t* fin = acce + 2;          // all MMAs of this CTA retired
   uint64_t* bfull = fin + 1;         // resident B (all K-slices) landed
-  uint64_t* rbar = bfull + 1;        // [kEpiWarps][2] residual tile landed
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rbar + 2 * kEpiWarps);
+  uint64_t* rbar = bfull + 1;        // [EW][2] residual tile landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(rbar + 2 * EW);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -119,11 +119,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; b++) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], kEpiWarps);
+      mbar_init(&acce[b], EW);
     }
     mbar_init(fin, 1);
     mbar_init(bfull, 1);
-    for (int k = 0; k < 2 * kEpiWarps; k++) mbar_init(&rbar[k], 1);
+    for (int k = 0; k < 2 * EW; k++) mbar_init(&rbar[k], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -234,18 +234,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- epilogue
     const Epi& e = a.epi;
     const int q = warp & 3;           // TMEM lane quarter this warp may read
-    const int half = (warp - 2) >> 2; // which interleaved half of the column chunks
+    // which of the EW / 4 interleaved sets of column chunks this warp stores
+    const int part = (warp - 2) >> 2;
+    constexpr int NPART = EW / 4;
     const int et = threadIdx.x - 64;  // 0..255 among the epilogue threads
     const int r = q * 32 + lane;      // tile row owned in the thread-per-row phases
     int* s_row = s_rows + (warp - 2) * 32 * 4 - q * 32 * 4;  // indexed by tile row q*32..q*32+31
     // Column vectors of this CTA's (fixed) N tile, loaded once.
-    for (int c = et; c < BN; c += 32 * kEpiWarps) {
+    for (int c = et; c < BN; c += 32 * EW) {
       const int col = n0 + c;
       s_vec[c] = e.bias ? e.bias[col] : 0.0f;
       s_vec[BN + c] = (e.ln_n > 0 && col < e.ln_n) ? e.ln_g[col] : 0.0f;
       s_vec[2 * BN + c] = (e.ln_n > 0 && col < e.ln_n) ? e.ln_b[col] : 0.0f;
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(32 * kEpiWarps) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * EW) : "memory");
     uint8_t* wbuf = obuf + (warp - 2) * WB;
     float* stg = reinterpret_cast<float*>(wbuf);  // STORE_SHUFFLE2 staging
     uint64_t* wrb = rbar + 2 * (warp - 2);        // this warp's residual barriers
@@ -295,11 +297,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Post-norm residual: the first chunk's tile is requested before the accumulator
     // is ready, so its latency hides behind the MMAs.
     if constexpr (STORE == STORE_ROWS && RES == 2) {
-      if (lane == 0 && half < BN / 32) {
+      if (lane == 0 && part < BN / 32) {
         bulk_wait_read<0>();
         const int jb = jcnt & 1;
         mbar_arrive_expect_tx(&wrb[jb], 4096);
-        box_load_res(wbuf + jb * 4096, n0 + half * 32, &wrb[jb]);
+        box_load_res(wbuf + jb * 4096, n0 + part * 32, &wrb[jb]);
       }
     }
 
@@ -352,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float nmr = -mean * rstd;
       const int sw128 = lane & 7, sw64 = (lane >> 1) & 3;  // this row's swizzle phases
 #pragma unroll 1
-      for (int c = half; c < BN / 32; c += 2, jcnt++) {
+      for (int c = part; c < BN / 32; c += NPART, jcnt++) {
         const int jb = jcnt & 1;
         float* f32 = reinterpret_cast<float*>(wbuf + jb * 4096);
         uint8_t* f16 = wbuf + F16OFF + jb * 2048;
@@ -507,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int wrow0 = q * 32;
       const int F = a.N / 4;  // STORE_SHUFFLE2: output channels
 #pragma unroll 1
-      for (int c = half; c < BN / 32; c += 2) {
+      for (int c = part; c < BN / 32; c += NPART) {
         float v[32];
         tmem_ld32(tbase + c * 32, v);
         const int cl0 = c * 32;
@@ -570,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if constexpr (STORE == STORE_PLANES) {
       float v[32];
       tmem_ld32(tbase, v);
-      if (valid && half == 0) {
+      if (valid && part == 0) {
 #pragma unroll
         for (int ch = 0; ch < 3; ch++) {
           const float x = pre(v[ch], ch);
@@ -586,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {  // STORE_DIRECT
       const int s = e.scale, s2 = s * s, nout = 3 * s2;
 #pragma unroll 1
-      for (int c = half; c < BN / 32; c += 2) {
+      for (int c = part; c < BN / 32; c += NPART) {
         float v[32];
         tmem_ld32(tbase + c * 32, v);
 #pragma unroll
@@ -620,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, int STAGES, int ACT, bool LN, int RES, int STORE, int AR = 0,
-          int WB = kWarpBuf, bool PATCH = false>
+          int WB = kWarpBuf, bool PATCH = false, int EW = kEpiWarps>
 cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const OutMaps& om,
                      const GemmArgs& a, cudaStream_t st) {
   constexpr int NA = AR > 0 ? AR : STAGES;
@@ -629,13 +631,13 @@ cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const Out
     return cudaErrorInvalidValue;
   if (AR > 0 && (a.conv || a.K / 64 > STAGES)) return cudaErrorInvalidValue;  // B not resident
   if (WB != kWarpBuf && (a.epi.o32 || a.epi.o32b)) return cudaErrorInvalidValue;
-  const size_t smem = 1024 + (size_t)NA * A_SLOT + (size_t)STAGES * B_SLOT + kEpiWarps * WB +
-                      3 * BN * 4 + kEpiWarps * 32 * 4 * 4 + (2 * NA + 6 + 2 * kEpiWarps) * 8 +
-                      16;
+  constexpr int threads = 64 + 32 * EW;
+  const size_t smem = 1024 + (size_t)NA * A_SLOT + (size_t)STAGES * B_SLOT + EW * WB +
+                      3 * BN * 4 + EW * 32 * 4 * 4 + (2 * NA + 6 + 2 * EW) * 8 + 16;
   static LaunchSetup setup;  // resident CTAs (SMs x CTAs per SM), per device
   int ctas = 0;
   const cudaError_t err = resident_ctas(
-      setup, k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH>, kThreads, smem, &ctas);
+      setup, k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH, EW>, threads, smem, &ctas);
   if (err != cudaSuccess) return err;
   const int NT = a.N / BN;
   const int tiles_m = a.conv ? a.B * a.tiles_x * a.tiles_y : (a.M + 127) / 128;
@@ -643,7 +645,7 @@ cudaError_t launch_t(const CUtensorMap& mapA, const CUtensorMap& mapB, const Out
   long G = tiles < ctas ? tiles : ctas;
   G = (G / NT) * NT;
   if (G < NT) G = NT;
-  return launch_pdl(k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH>, dim3((unsigned)G), dim3(kThreads), smem,
+  return launch_pdl(k_gemm<BN, STAGES, ACT, LN, RES, STORE, AR, WB, PATCH, EW>, dim3((unsigned)G), dim3(threads), smem,
                     st, mapA, mapB, om, a);
 }
 
@@ -691,8 +693,10 @@ cudaError_t launch_gemm(const CUtensorMap& mapA, const CUtensorMap& mapB, const 
   S2S_VARIANT(192, 3, ACT_NONE, false, 2, STORE_ROWS)
   // QKV (fp16 output only, B resident): A gets a six-slot ring of its own; with
   // two-term operands (K = 3 x 192) B streams through the ring
+  // twelve epilogue warps: each stores 2 of the tile's 6 column chunks
   if (BN == 192 && act == ACT_QKNORM && !ln && res == 0 && store == STORE_ROWS && a.K / 64 <= 3)
-    return launch_t<192, 3, ACT_QKNORM, false, 0, STORE_ROWS, 6, kWarpBufF16>(mapA, mapB, om, a, st);
+    return launch_t<192, 3, ACT_QKNORM, false, 0, STORE_ROWS, 6, kWarpBufF16, false, 12>(
+        mapA, mapB, om, a, st);
   if (BN == 192 && act == ACT_QKNORM && !ln && res == 0 && store == STORE_ROWS)
     return launch_t<192, 3, ACT_QKNORM, false, 0, STORE_ROWS, 0, kWarpBufF16>(mapA, mapB, om, a, st);
   S2S_VARIANT(96, 4, ACT_QKNORM, false, 0, STORE_ROWS)
