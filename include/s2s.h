@@ -142,6 +142,15 @@ int64_t s2s_launch_count(const s2s_handle* h);
 int s2s_debug_stop_after(s2s_handle* h, int64_t launches);
 int64_t s2s_debug_read(s2s_handle* h, const char* buffer, float* host, int64_t capacity);
 
+/* Diagnostics of the peer-store halo transport on one GPU (no counterpart in the
+ * reference): two exchanges of `rows` rows (1..8) on a scratch band plane whose
+ * neighbours on both sides are the plane itself, through the kernel, flags and
+ * epochs a sharded forward uses - its last rows must land in its top halo and its
+ * first rows in its bottom halo. With `missing` != 0 the neighbours' mailbox is one
+ * that no kernel serves, so the exchange's waits run out after about a second:
+ * S2S_ERR_TIMEOUT, and the handle stays usable. */
+int s2s_debug_halo_loopback(s2s_handle* h, int rows, int missing);
+
 /* ---- Row-band sharding of one image across GPUs. No counterpart in the
  * reference, which runs an image on one GPU (src/gpu.rs:462-583 is the forward
  * each band repeats). The padded plane's window rows are split into contiguous

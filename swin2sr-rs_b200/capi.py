@@ -26,7 +26,7 @@ UPSAMPLER_CODE = {"pixelshuffle": 0, "pixelshuffledirect": 1, "nearest+conv": 2,
 EXPORTS = ("s2s_create", "s2s_forward", "s2s_forward_batch", "s2s_forward_device",
            "s2s_aux_dims", "s2s_uploaded_bytes", "s2s_workspace_bytes", "s2s_last_error",
            "s2s_profile_enable", "s2s_profile_report", "s2s_launch_count", "s2s_destroy",
-           "s2s_version", "s2s_debug_stop_after", "s2s_debug_read",
+           "s2s_version", "s2s_debug_stop_after", "s2s_debug_read", "s2s_debug_halo_loopback",
            "s2s_window_attention_noalloc", "s2s_band_unique_id", "s2s_band_init",
            "s2s_band_init_local", "s2s_band_rows", "s2s_forward_band", "s2s_forward_band_host",
            "s2s_band_partition", "s2s_band_halo_ops", "s2s_png_header", "s2s_png_decode",
@@ -98,6 +98,8 @@ def load() -> ctypes.CDLL:
     L.s2s_debug_stop_after.restype = ctypes.c_int
     L.s2s_debug_read.argtypes = [vp, ctypes.c_char_p, fp, ctypes.c_int64]
     L.s2s_debug_read.restype = ctypes.c_int64
+    L.s2s_debug_halo_loopback.argtypes = [vp, ctypes.c_int, ctypes.c_int]
+    L.s2s_debug_halo_loopback.restype = ctypes.c_int
     L.s2s_window_attention_noalloc.argtypes = [vp] + [ctypes.c_int] * 5 + [vp, vp, ctypes.c_int,
                                                                           vp]
     L.s2s_window_attention_noalloc.restype = ctypes.c_int
@@ -271,6 +273,10 @@ class Handle:
 
     def debug_stop_after(self, launches: int):
         self._check(self.L.s2s_debug_stop_after(self.h, int(launches)))
+
+    def debug_halo_loopback(self, rows: int, missing: bool = False) -> None:
+        """One-GPU check of the peer-store halo kernel (s2s_debug_halo_loopback)."""
+        self._check(self.L.s2s_debug_halo_loopback(self.h, int(rows), int(bool(missing))))
 
     def debug_read(self, name: str) -> np.ndarray:
         n = self.L.s2s_debug_read(self.h, name.encode(), None, 0)

@@ -1018,7 +1018,8 @@ void halo_exchange(s2s_handle* H, Plan* P, __half* buf, int ld, int n, bool cycl
     const bool has_prev = cyclic || P->rank != 0, has_next = cyclic || P->rank != P->world - 1;
     ck(launch_halo_push(buf, has_prev ? peer_plane(P->prevp) : nullptr,
                         has_next ? peer_plane(P->nextp) : nullptr, P->mb, &P->prevp, &P->nextp,
-                        row * 2, n, P->halo, P->own_rows, zero_edges, zero_edges, st),
+                        row * 2, n, P->halo, P->own_rows, zero_edges, zero_edges, st,
+                        10000000000ull, false),
        "halo push");
     H->launches++;
     return;
@@ -1861,6 +1862,60 @@ int s2s_profile_report(s2s_handle* H, char* buf, int cap, int reset) {
 }
 
 int64_t s2s_launch_count(const s2s_handle* H) { return H ? H->launches.load() : 0; }
+
+int s2s_debug_halo_loopback(s2s_handle* H, int rows, int missing) {
+  if (!H) return S2S_ERR_INVALID;
+  return guarded(H, [&] {
+    if (rows < 1 || rows > 8) fail(S2S_ERR_INVALID, "s2s_debug_halo_loopback: rows must be in [1, 8]");
+    ck(cudaStreamSynchronize(H->stream), "halo loopback");
+    // a band plane of 16 owned rows between two 8-row halos, 1 KB a row
+    const int halo = 8, own = 16, hp = own + 2 * halo;
+    const size_t rb = 1024, plane = (size_t)hp * rb;
+    struct Scratch {
+      void* p = nullptr;
+      ~Scratch() {
+        if (p) cudaFree(p);
+      }
+    } d;
+    ck(cudaMalloc(&d.p, plane + 2 * sizeof(HaloMailbox)), "halo loopback scratch");
+    uint8_t* dplane = static_cast<uint8_t*>(d.p);
+    HaloMailbox* mine = reinterpret_cast<HaloMailbox*>(dplane + plane);
+    HaloMailbox* nobody = mine + 1;  // a neighbour that never runs
+    std::vector<uint8_t> h(plane, 0);
+    for (int r = halo; r < halo + own; r++)
+      for (size_t c = 0; c < rb; c++) h[r * rb + c] = (uint8_t)((r * 131 + c * 7 + 1) & 0xff);
+    ck(cudaMemcpy(dplane, h.data(), plane, cudaMemcpyHostToDevice), "halo loopback");
+    ck(cudaMemset(mine, 0, 2 * sizeof(HaloMailbox)), "halo loopback");
+    // both neighbours are this plane; with `missing` their mailbox is one nobody serves
+    HaloPeer self;
+    self.x16 = dplane;
+    self.mb = missing ? nobody : mine;
+    self.halo = halo;
+    self.own_rows = own;
+    for (int e = 1; e <= 2; e++) {
+      ck(launch_halo_push(dplane, dplane, dplane, mine, &self, &self, rb, rows, halo, own, false,
+                          false, H->stream, 1000000000ull, true),
+         "halo loopback");
+      ck(cudaStreamSynchronize(H->stream), "halo loopback");
+      check_device_error(H);
+      unsigned seq = 0;
+      ck(cudaMemcpy(&seq, &mine->seq, sizeof seq, cudaMemcpyDeviceToHost), "halo loopback");
+      if (seq != (unsigned)e)
+        fail(S2S_ERR_CUDA, "halo loopback: exchange " + std::to_string(e) + " left epoch " +
+                               std::to_string(seq));
+    }
+    std::vector<uint8_t> out(plane);
+    ck(cudaMemcpy(out.data(), dplane, plane, cudaMemcpyDeviceToHost), "halo loopback");
+    // top halo <- the last `rows` owned rows, bottom halo <- the first; the rest as sent
+    for (int r = 0; r < hp; r++) {
+      int src = r;
+      if (r >= halo - rows && r < halo) src = r + own;
+      else if (r >= halo + own && r < halo + own + rows) src = r - own;
+      if (memcmp(out.data() + r * rb, h.data() + (size_t)src * rb, rb) != 0)
+        fail(S2S_ERR_CUDA, "halo loopback: plane row " + std::to_string(r) + " differs");
+    }
+  });
+}
 
 int s2s_debug_stop_after(s2s_handle* H, int64_t launches) {
   if (!H) return S2S_ERR_INVALID;

@@ -15,8 +15,8 @@
 //      it expects rows from, so the kernel completes only once R's halo is filled;
 //      without a neighbour (non-cyclic edges) the halo rows are zeroed when asked;
 //   4. the last block to finish records e as R's completed exchange.
-// Every wait is bounded (DEV_TIMEOUT_HALO after ~10 s, or at once when another wait
-// of the library already gave up); the host then fails the forward.
+// Every wait is bounded (DEV_TIMEOUT_HALO after ~10 s in a forward, or at once when
+// another wait of the library already gave up); the host then fails the forward.
 #include "common.cuh"
 #include "halo.cuh"
 
@@ -36,6 +36,7 @@ struct HaloPushArgs {
   int next_halo;           // the next band's top halo ends at its row next_halo
   int prev_end;            // the previous band's bottom halo starts at its row prev_end
   int zero_top, zero_bottom;  // no neighbour on that side: zero this rank's halo rows
+  uint64_t limit_ns;          // how long each wait may last
 };
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
@@ -48,13 +49,13 @@ __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Wait until *p has reached epoch e (wrap-safe), for at most ~10 s of wall time.
-__device__ bool wait_epoch(const unsigned* p, unsigned e) {
+// Wait until *p has reached epoch e (wrap-safe), for at most limit_ns of wall time.
+__device__ bool wait_epoch(const unsigned* p, unsigned e, uint64_t limit_ns) {
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 0;; ++it) {
     if ((int)(ld_acquire_sys(p) - e) >= 0) return true;
     if ((it & 63u) == 63u) {
-      if (global_timer_ns() - t0 > 10000000000ull) {
+      if (global_timer_ns() - t0 > limit_ns) {
         record_error(DEV_TIMEOUT_HALO);
         return false;
       }
@@ -76,8 +77,8 @@ __global__ void __launch_bounds__(128) k_halo_push(const HaloPushArgs a) {
       if (a.next_mb) st_release_sys(&a.next_mb->may_push_prev, e);
     }
     bool ok = true;
-    if (a.next_dst) ok = wait_epoch(&a.mine->may_push_next, e);
-    if (ok && a.prev_dst) ok = wait_epoch(&a.mine->may_push_prev, e);
+    if (a.next_dst) ok = wait_epoch(&a.mine->may_push_next, e, a.limit_ns);
+    if (ok && a.prev_dst) ok = wait_epoch(&a.mine->may_push_prev, e, a.limit_ns);
     s_ok = ok;
   }
   __syncthreads();
@@ -108,8 +109,8 @@ __global__ void __launch_bounds__(128) k_halo_push(const HaloPushArgs a) {
     // this rank's halo: the top rows from the previous band, the bottom from the next
     if (threadIdx.x < kHaloBlocks) {
       bool ok = true;
-      if (a.prev_dst) ok = wait_epoch(&a.mine->top_in[threadIdx.x], e);
-      if (ok && a.next_dst) wait_epoch(&a.mine->bottom_in[threadIdx.x], e);
+      if (a.prev_dst) ok = wait_epoch(&a.mine->top_in[threadIdx.x], e, a.limit_ns);
+      if (ok && a.next_dst) wait_epoch(&a.mine->bottom_in[threadIdx.x], e, a.limit_ns);
     }
     __syncthreads();
   }
@@ -128,11 +129,13 @@ __global__ void __launch_bounds__(128) k_halo_push(const HaloPushArgs a) {
 
 // One exchange of `n` rows of the plane `buf` (row_bytes per row) with the
 // neighbours `prev` / `next` (their copy of the same plane: prev_buf / next_buf;
-// null when this rank has no such neighbour in this exchange).
+// null when this rank has no such neighbour in this exchange). `cooperative`: the
+// blocks are launched together (the loopback diagnostic, where they wait on each
+// other's flags).
 cudaError_t launch_halo_push(const void* buf, void* prev_buf, void* next_buf, HaloMailbox* mine,
                              const HaloPeer* prev, const HaloPeer* next, size_t row_bytes, int n,
                              int halo, int own_rows, bool zero_top, bool zero_bottom,
-                             cudaStream_t st) {
+                             cudaStream_t st, uint64_t limit_ns, bool cooperative) {
   if (row_bytes % 16 != 0 || n < 1 || n > halo || n > own_rows)
     return cudaErrorInvalidValue;
   HaloPushArgs a;
@@ -150,6 +153,12 @@ cudaError_t launch_halo_push(const void* buf, void* prev_buf, void* next_buf, Ha
   a.prev_end = prev_buf ? prev->halo + prev->own_rows : 0;
   a.zero_top = zero_top && !prev_buf;
   a.zero_bottom = zero_bottom && !next_buf;
+  a.limit_ns = limit_ns;
+  if (cooperative) {
+    void* args[] = {&a};
+    return cudaLaunchCooperativeKernel((const void*)k_halo_push, dim3(kHaloBlocks), dim3(128), args,
+                                       0, st);
+  }
   k_halo_push<<<kHaloBlocks, 128, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -120,3 +120,36 @@ def test_band_mode_rejects_the_aux_head_and_whole_image_calls():
     finally:
         for h in hs:
             h.close()
+
+
+@pytest.mark.parametrize("rows", [1, 4, 8])
+def test_peer_store_halo_kernel_in_loopback(rows):
+    """The peer-store exchange kernel on one GPU, its neighbours being the plane itself:
+    the last `rows` owned rows land in the top halo, the first in the bottom halo, and
+    the device-side exchange epoch advances once per exchange (checked inside
+    s2s_debug_halo_loopback)."""
+    C = capi()
+    H = C.Handle(pkg().weights.Weights.seeded("lightweight_sr", 0, True))
+    try:
+        H.debug_halo_loopback(rows)
+    finally:
+        H.close()
+
+
+def test_peer_store_halo_wait_runs_out_without_a_neighbour():
+    """No neighbour ever signals: the kernel's bounded waits give up after about a
+    second, the call reports S2S_ERR_TIMEOUT, and the handle (and its context) still
+    works afterwards."""
+    import time
+    C = capi()
+    H = C.Handle(pkg().weights.Weights.seeded("lightweight_sr", 0, True))
+    try:
+        t0 = time.time()
+        with pytest.raises(C.S2SError) as ei:
+            H.debug_halo_loopback(4, missing=True)
+        assert "S2S_ERR_TIMEOUT" in str(ei.value) or ei.value.code == 5, ei.value
+        assert time.time() - t0 < 30.0
+        H.debug_halo_loopback(4)
+    finally:
+        H.close()
+
