@@ -271,10 +271,11 @@ def main():
         mode = "single"
     x = wl.make_input(args.workload)
     if mode == "batch":
-        if B % world:
-            raise SystemExit(f"batch {B} does not split over {world} ranks")
-        bl = B // world
-        x = x[rank * bl:(rank + 1) * bl]
+        try:
+            lo, hi = wl.batch_shard(B, world, rank)
+        except ValueError as e:
+            raise SystemExit(str(e))
+        x = x[lo:hi]
     xa = wl.adjust(x, wt)
     Bl = xa.shape[0]                       # images this rank processes
     handle = capi.Handle(wt, device=local)

@@ -67,6 +67,19 @@ def make_input(name: str, batch: int | None = None) -> np.ndarray:
     raise KeyError(name)
 
 
+def batch_shard(batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Images [lo, hi) of a batch that rank ``rank`` of ``world`` runs in the batch
+    data-parallel mode: contiguous, equal shards in rank order, so the ranks' outputs
+    concatenate to the batch's. The images are independent (no exchange); a batch
+    that does not divide evenly is refused, so every rank times the same work."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if batch % world:
+        raise ValueError(f"batch {batch} does not split over {world} ranks")
+    n = batch // world
+    return rank * n, (rank + 1) * n
+
+
 def adjust(x: np.ndarray, wt) -> np.ndarray:
     """Pre::adjust over a batch: (x - mean) * img_range (src/backend.rs:76-86)."""
     m = np.asarray(wt.mean, np.float32)[None, :, None, None]
