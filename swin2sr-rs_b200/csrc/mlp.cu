@@ -3,9 +3,9 @@
 // one persistent tcgen05 kernel over 128-token tiles. The hidden dimension is
 // walked in 64-column parts j = 0 .. NP-1:
 //   fc1 part j   D1[j % 2] (64 TMEM columns) = X16 tile * W1[64j : 64j+64]^T
-//   epi-1 part j bias + erf-GELU, fp16, into hidden chunk buffer j % 2 in shared
-//                memory (128-byte-swizzled K-major: fc2's A operand)
-//   fc2 chunk j  D2[tile % 2] += hidden chunk j * W2[:, 64j : 64j+64]^T
+//   epi-1 part j bias + erf-GELU, fp16, back into D1[j % 2] in TMEM over the columns
+//                each warp has read (two fp16 per 32-bit column: fc2's A operand)
+//   fc2 chunk j  D2[tile % 2] += hidden chunk j (A from TMEM) * W2[:, 64j : 64j+64]^T
 // and once all parts are in, epilogue 2 applies bias, LayerNorm over the real C
 // columns and the residual, and rewrites fp32 X and fp16 X16 in place by TMA stores.
 // The MMA warp issues fc1 part j+2 right after fc2 chunk j, so the tensor core always
@@ -34,6 +34,31 @@ namespace {
 constexpr int kMlpThreads = 576;
 constexpr int kMlpEpiWarps = 8;  // per epilogue group
 constexpr int kMlpPart = 64;  // hidden columns per part
+
+// D(tmem) (+)= A(tmem) * B(smem desc)^T, fp16 inputs, fp32 accumulate. A (M = 128 rows,
+// K-major) sits in TMEM as the rows' lanes, two fp16 K elements per 32-bit column.
+__device__ __forceinline__ void tc_mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns from this warp's registers into TMEM, and
+// the wait for the store to complete.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
 
 template <int CP, int HP, int STAGES>
 struct MlpCfg {
@@ -271,12 +296,14 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
             ok = false;
             break;
           }
-          const uint64_t ad = sw128_desc(smem_u32(sH + (j & 1) * 16384));
+          // hidden chunk j: K 0-31 at D1 columns 0-15, K 32-63 at columns 32-47 of
+          // buffer j % 2; a K = 16 step takes 8 columns
+          const uint32_t ha = tmem + (uint32_t)((j & 1) * kMlpPart);
           const uint64_t bd = sw128_desc(smem_u32(ring + s * Cfg::SLOT));
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
-            tc_mma_f16(d2, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), id2,
-                       (j | kk) != 0 ? 1u : 0u);
+            tc_mma_f16_ta(d2, ha + (uint32_t)((kk >> 1) * 32 + (kk & 1) * 8),
+                          bd + (uint64_t)(kk * 2), id2, (j | kk) != 0 ? 1u : 0u);
           tc_commit(&empty[s]);
           kit++;
           if (j + 2 < NP) ok = fc1(j + 2);
@@ -334,16 +361,10 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
             hv[2 * u] = *reinterpret_cast<const uint32_t*>(&h0);
             hv[2 * u + 1] = *reinterpret_cast<const uint32_t*>(&h1);
           }
-          uint8_t* chunk = sH + (j & 1) * 16384;
-#pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const int uu = (half * 4 + u) ^ (r & 7);
-            *reinterpret_cast<uint4*>(chunk + r * 128 + uu * 16) =
-                make_uint4(hv[4 * u], hv[4 * u + 1], hv[4 * u + 2], hv[4 * u + 3]);
-          }
-          // generic-proxy writes -> visible to the tensor core (async proxy); the D1
-          // buffer is drained
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          // the fp16 hidden values go back into TMEM over this warp's own (already read)
+          // fp32 columns: hidden column 32 * half + 2c + e at D1 column 32 * half + c,
+          // half e - fc2's A operand
+          tmem_st16(tq + (uint32_t)((j & 1) * kMlpPart + half * 32), hv);
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&hfull[j & 1]);
