@@ -73,7 +73,7 @@ struct MlpCfg {
   // epilogue 2 per warp: two fp32 32x32 tiles (residual in / result out, 128-byte
   // swizzle) and one fp16 tile (64-byte swizzle)
   static constexpr int STG = 2 * 4096 + 2048;
-  static constexpr size_t SMEM = 1024 + (size_t)KC1 * 16384 + 2 * 16384 +
+  static constexpr size_t SMEM = 1024 + (size_t)KC1 * 16384 +
                                  (size_t)STAGES * SLOT + (size_t)kMlpEpiWarps * STG +
                                  (HP + 6 * CP) * 4 + (2 * STAGES + 16 + 2 * kMlpEpiWarps) * 8 +
                                  16;
@@ -94,15 +94,14 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sX = smem;                           // KC1 chunks: the X16 (PROJ: AO, then x1) tile
-  uint8_t* sH = sX + KC1 * 16384;               // 2 hidden chunk buffers (16 KB each)
-  uint8_t* ring = sH + 2 * 16384;
+  uint8_t* ring = sX + KC1 * 16384;
   uint8_t* stgbuf = ring + STAGES * Cfg::SLOT;  // [kMlpEpiWarps][STG] epilogue staging
   // b1, b2, g2, beta2, bp, g1, beta1
   float* s_vec = reinterpret_cast<float*>(stgbuf + kMlpEpiWarps * Cfg::STG);
   uint64_t* full = reinterpret_cast<uint64_t*>(s_vec + HP + 6 * CP);
   uint64_t* empty = full + STAGES;
   uint64_t* acc1 = empty + STAGES;   // [2] fc1 part in D1 buffer b
-  uint64_t* hfull = acc1 + 2;        // [2] hidden chunk buffer b written (8 warp arrivals)
+  uint64_t* hfull = acc1 + 2;        // [2] fp16 hidden chunk in D1 buffer b (8 warp arrivals)
   uint64_t* acc2 = hfull + 2;        // [2] D2 buffer d complete
   uint64_t* d2free = acc2 + 2;       // [2] D2 buffer d drained (8 warp arrivals)
   uint64_t* xfull = d2free + 2;      // X16 (AO) tile landed
