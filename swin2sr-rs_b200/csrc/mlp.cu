@@ -623,11 +623,11 @@ cudaError_t launch_mlp(const CUtensorMap& mX, const CUtensorMap& mW1, const CUte
                        int hp, cudaStream_t st, const CUtensorMap* mWp) {
   if (mWp) {
     if (cp == 192 && hp == 384 && a.bp && a.g1 && a.beta1)
-      return launch_mlp_t<192, 384, 2, true>(mX, mW1, mW2, mX32, mX16o, *mWp, a, st);
+      return launch_mlp_t<192, 384, 3, true>(mX, mW1, mW2, mX32, mX16o, *mWp, a, st);
     return cudaErrorNotSupported;
   }
   if (cp == 192 && hp == 384)
-    return launch_mlp_t<192, 384, 2, false>(mX, mW1, mW2, mX32, mX16o, mX, a, st);
+    return launch_mlp_t<192, 384, 3, false>(mX, mW1, mW2, mX32, mX16o, mX, a, st);
   if (cp == 64 && hp == 128)
     return launch_mlp_t<64, 128, 4, false>(mX, mW1, mW2, mX32, mX16o, mX, a, st);
   return cudaErrorNotSupported;
