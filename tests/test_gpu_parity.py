@@ -84,6 +84,24 @@ def test_forward_matches_oracle(task, h, w):
         check(gpu.aux(), raux, f"{task} {h}x{w} aux")
 
 
+@pytest.mark.parametrize("size", [56, 64, 128])
+@pytest.mark.parametrize("task", ["classical_sr_x2", "classical_sr", "compressed_sr"])
+def test_square_sizes_across_tile_boundaries(task, size):
+    """The reference's GPU-against-CPU sizes (tests/gpu.rs:96-173): 56, 64 and 128
+    pixels square, below and above a 64-wide boundary, for the pixel-shuffle heads and
+    the compressed head with its aux plane; here against the oracle, perturbed weights."""
+    O = oracle()
+    wt, gpu = backend_for(task, 0, True)
+    rng = np.random.default_rng(size * 7 + len(task))
+    x = rng.random((3, size, size), dtype=np.float32)
+    a = adjust(wt, x)
+    out = gpu.forward(size, size, a)
+    ref, raux = O.forward(wt, size, size, a)
+    check(out, ref, f"{task} {size}x{size}")
+    if raux is not None:
+        check(gpu.aux(), raux, f"{task} {size}x{size} aux")
+
+
 def test_batch_members_equal_single_runs():
     """A batch is independent images: every member equals its own single-image run."""
     wt, gpu = backend_for("compressed_sr", 0, True)
