@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
         }
         ok = fc1(0) && fc1(1);
         for (int j = 0; j < NP && ok; j++) {
-          // hidden chunk j written (and D1 buffer j % 2 drained) by epilogue 1
+          // hidden chunk j (fp16, in D1 buffer j % 2) written by epilogue 1
           if (!mbar_wait(&hfull[j & 1], (uint32_t)((i * (NP / 2) + (j >> 1)) & 1), DEV_TIMEOUT_ACC)) {
             ok = false;
             break;
@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1)
     asm volatile("bar.sync 1, %0;" ::"r"(64 * kMlpEpiWarps) : "memory");
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     if (gelu_group) {
-      // ---- epilogue 1: hidden chunk j = GELU(D1 + b1) -> fp16 -> shared
+      // ---- epilogue 1: hidden chunk j = GELU(D1 + b1) -> fp16 -> back into D1 (TMEM)
       int i = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, i++) {
