@@ -293,7 +293,11 @@ def test_pinned_output_buffers_are_written_directly(task):
 def test_unfused_mlp_path_matches_the_fused_kernel(task, monkeypatch):
     """S2S_UNFUSED_MLP (read at create) runs the MLP as two GEMMs with the hidden in
     HBM: the same fp16 hidden, the same fc2 K order, so the output must agree with
-    the fused kernel to rounding."""
+    the fused kernel to rounding. The 60-wide network runs single-term operands here
+    (S2S_SPLIT=0): with its default two-term operands the MLP is always two GEMMs, and
+    the 64-channel fused kernel would go untested."""
+    if task == "lightweight_sr":
+        monkeypatch.setenv("S2S_SPLIT", "0")
     capi = importlib.import_module("swin2sr_b200.capi")
     P = pkg()
     wt = P.weights.Weights.seeded(task, 0, True)
@@ -301,6 +305,10 @@ def test_unfused_mlp_path_matches_the_fused_kernel(task, monkeypatch):
     H = capi.Handle(wt)
     try:
         fused = H.forward_batch(x)[0]
+        H.profile(True)
+        H.forward_batch(x)
+        rep = H.profile_report()
+        assert ("mlp_fused" in rep or "proj_mlp" in rep) and "gemm_fc1" not in rep
     finally:
         H.close()
     monkeypatch.setenv("S2S_UNFUSED_MLP", "1")
